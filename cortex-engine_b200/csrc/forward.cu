@@ -1,0 +1,257 @@
+// Whole-forward driver: CortexModel.forward (cortex/models/cortex.py:90-122),
+// return_aux=False, launched as one stream of kernels with no host sync.
+//
+//   pack            counts/offsets/dest of the flat events     (_pack_events, :125-165)
+//   tokenize+LN_kv  gather-sum straight into packed order, norm_kv fused
+//   LN_q, q_proj    batch-invariant latent queries, computed once per forward
+//   kv_proj         packed (E, 2D) keys|values                 (perceiver.py:67-69)
+//   cross attention varlen keys per sample, no padding          (perceiver.py:71-80)
+//   out_proj+resid  latents param broadcast as the residual      (perceiver.py:82)
+//   N x block       LN, qkv, attention, out+resid, LN, mlp0+GELU, mlp2+resid
+//   final LN + head LN (one pass), head q (batch-invariant), head kv_proj,
+//   2-query attention, out_proj D->1                           (cortex.py:29-53)
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ck {
+int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
+                    int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale,
+                    int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
+                    int64_t ldy, cudaStream_t st);
+int attention_dispatch(const ck_attention_args& a, cudaStream_t st);
+}  // namespace ck
+
+using namespace ck;
+
+namespace {
+
+constexpr float kLnEps = 1e-5f;
+
+size_t al(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+  size_t counts, offsets, dest, emax, packws, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
+      total;
+};
+
+Layout plan(const ck_model* m, int64_t E, int32_t B) {
+  const size_t es = m->dtype == CK_F32 ? 4 : 2;
+  const size_t D = m->latent_dim, Dh_in = m->hidden_dim, L = m->num_latents;
+  const size_t BL = (size_t)B * L;
+  Layout o;
+  size_t p = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = p;
+    p += al(bytes);
+    return at;
+  };
+  o.counts = take((size_t)B * 4);
+  o.offsets = take((size_t)(B + 1) * 4);
+  o.dest = take((size_t)(E > 0 ? E : 1) * 4);
+  o.emax = take(4);
+  o.packws = take(pack_workspace_bytes(E, B));
+  o.xkv = take((size_t)(E > 0 ? E : 1) * Dh_in * es);
+  o.kv = take((size_t)(E > 0 ? E : 1) * 2 * D * es);
+  o.xq = take(L * D * es);
+  o.qc = take(L * D * es);
+  o.lat = take(BL * D * es);
+  o.x = take(BL * D * es);
+  o.qkv = take(BL * 3 * D * es);
+  o.att = take(BL * D * es);
+  o.hbuf = take(BL * (size_t)m->mlp_hidden * es);
+  o.qh = take((size_t)m->behavior_dim * D * es);
+  o.oh = take((size_t)B * m->behavior_dim * D * es);
+  o.total = p;
+  return o;
+}
+
+int lin(const ck_model* m, const void* A, int64_t M, int64_t K, int64_t lda,
+        const ck_linear_weight& w, int64_t N, int epi, const void* aux, int64_t ld_aux,
+        int64_t mod, void* Y, int64_t ldy, cudaStream_t st) {
+  if (w.w == nullptr) return CK_ERR_INVALID_ARG;
+  if (w.bias != nullptr) return CK_ERR_UNSUPPORTED;  // every linear on this path is bias-free
+  const int wd = w.dtype;
+  if (wd != m->dtype && wd != CK_I8) return CK_ERR_UNSUPPORTED;
+  return linear_dispatch(A, m->dtype, M, K, lda, w.w, wd, CK_W_NK, N, K, w.scale, epi, aux,
+                         ld_aux, mod, Y, ldy, st);
+}
+
+ck_attention_args attn_base(const ck_model* m) {
+  ck_attention_args a;
+  memset(&a, 0, sizeof(a));
+  a.dtype = m->dtype;
+  return a;
+}
+
+}  // namespace
+
+extern "C" size_t ck_forward_workspace_bytes(const ck_model* m, int64_t E, int32_t B) {
+  if (m == nullptr || B <= 0 || E < 0) return 0;
+  return plan(m, E, B).total + 256;
+}
+
+extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, const void* val,
+                          const void* bidx, int idx_dt, int64_t E, int32_t B, void* out, void* ws,
+                          size_t ws_bytes, void* stream) {
+  if (m == nullptr || out == nullptr || B <= 0 || E < 0) return CK_ERR_INVALID_ARG;
+  if (m->dtype != CK_BF16 && m->dtype != CK_F32) return CK_ERR_UNSUPPORTED;
+  if (m->latent_dim <= 0 || m->hidden_dim <= 0 || m->num_latents <= 0 || m->num_heads <= 0 ||
+      m->cross_heads <= 0 || m->head_dim <= 0 || m->mlp_hidden <= 0 || m->behavior_dim <= 0 ||
+      m->num_layers < 0)
+    return CK_ERR_INVALID_ARG;
+  if (m->num_heads * m->head_dim != m->latent_dim) return CK_ERR_INVALID_ARG;
+  if (m->latent_dim % m->cross_heads != 0) return CK_ERR_INVALID_ARG;
+  if (m->num_layers > 0 && m->blocks == nullptr) return CK_ERR_INVALID_ARG;
+  if (E > 0 && (!nid || !tb || !val || !bidx)) return CK_ERR_INVALID_ARG;
+  const Layout lay = plan(m, E, B);
+  if (ws == nullptr || ws_bytes < lay.total + 256) return CK_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+  auto P = [&](size_t off) { return reinterpret_cast<void*>(base + off); };
+  int32_t* counts = reinterpret_cast<int32_t*>(P(lay.counts));
+  int32_t* offsets = reinterpret_cast<int32_t*>(P(lay.offsets));
+  int32_t* dest = reinterpret_cast<int32_t*>(P(lay.dest));
+  int32_t* emax = reinterpret_cast<int32_t*>(P(lay.emax));
+  const int64_t D = m->latent_dim, Din = m->hidden_dim, L = m->num_latents;
+  const int64_t BL = (int64_t)B * L;
+  const int64_t H = m->num_heads, Dh = m->head_dim;
+  const int64_t Hc = m->cross_heads, Dhc = D / Hc;
+  const int64_t nq = m->behavior_dim;
+  int rc;
+#define CK_TRY(expr)           \
+  do {                         \
+    rc = (expr);               \
+    if (rc != CK_OK) return rc; \
+  } while (0)
+
+  // 1. packing
+  CK_TRY(pack_events(bidx, idx_dt, 1, E, B, counts, offsets, dest, emax, P(lay.packws),
+                     pack_workspace_bytes(E, B), st));
+  // 2. tokenizer + norm_kv, written in packed order
+  CK_TRY(tokenize(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din, m->n_vocab,
+                  m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1, 1, 1, E, dest,
+                  m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st));
+  // 3. latent queries (batch-invariant)
+  CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
+                  CK_NORM_LAYER, P(lay.xq), D, st));
+  CK_TRY(lin(m, P(lay.xq), L, D, D, m->cross_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qc), D, st));
+  // 4. packed keys|values
+  if (E > 0)
+    CK_TRY(lin(m, P(lay.xkv), E, Din, Din, m->cross_kv, 2 * D, CK_EPI_STORE, nullptr, 0, 0,
+               P(lay.kv), 2 * D, st));
+  // 5. cross attention over each sample's own events
+  {
+    const size_t es_b = m->dtype == CK_F32 ? 4 : 2;
+    ck_attention_args a = attn_base(m);
+    a.B = B;
+    a.H = (int32_t)Hc;
+    a.Dh = (int32_t)Dhc;
+    a.Lq = (int32_t)L;
+    a.key_offsets = offsets;
+    a.q = P(lay.qc);
+    a.q_ld = D;
+    a.q_rows = L;
+    a.q_col_per_h = Dhc;
+    a.k = P(lay.kv);
+    a.k_ld = 2 * D;
+    a.k_rows = E > 0 ? E : 1;
+    a.k_col_per_h = Dhc;
+    a.v = reinterpret_cast<uint8_t*>(P(lay.kv)) + D * es_b;
+    a.v_ld = 2 * D;
+    a.v_rows = E > 0 ? E : 1;
+    a.v_col_per_h = Dhc;
+    a.o = P(lay.att);
+    a.o_ld = D;
+    a.o_rows_per_b = L;
+    a.o_col_per_h = Dhc;
+    a.scale = 1.0f / sqrtf((float)Dhc);
+    CK_TRY(attention_dispatch(a, st));
+  }
+  // 6. out_proj + broadcast latent residual
+  CK_TRY(lin(m, P(lay.att), BL, D, D, m->cross_out, D, CK_EPI_RESID, m->latents, D, L, P(lay.lat),
+             D, st));
+  // 7. self-attention blocks
+  const size_t es_b = m->dtype == CK_F32 ? 4 : 2;
+  for (int i = 0; i < m->num_layers; ++i) {
+    const ck_block_weights& w = m->blocks[i];
+    CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b, kLnEps,
+                    CK_NORM_LAYER, P(lay.x), D, st));
+    CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
+               3 * D, st));
+    ck_attention_args a = attn_base(m);
+    a.B = B;
+    a.H = (int32_t)H;
+    a.Dh = (int32_t)Dh;
+    a.Lq = (int32_t)L;
+    a.n_keys = (int32_t)L;
+    a.q = P(lay.qkv);
+    a.q_ld = 3 * D;
+    a.q_rows = BL;
+    a.q_rows_per_b = L;
+    a.q_col_per_h = Dh;
+    a.k = reinterpret_cast<uint8_t*>(P(lay.qkv)) + D * es_b;
+    a.k_ld = 3 * D;
+    a.k_rows = BL;
+    a.k_rows_per_b = L;
+    a.k_col_per_h = Dh;
+    a.v = reinterpret_cast<uint8_t*>(P(lay.qkv)) + 2 * D * es_b;
+    a.v_ld = 3 * D;
+    a.v_rows = BL;
+    a.v_rows_per_b = L;
+    a.v_col_per_h = Dh;
+    a.o = P(lay.att);
+    a.o_ld = D;
+    a.o_rows_per_b = L;
+    a.o_col_per_h = Dh;
+    a.scale = 1.0f / sqrtf((float)Dh);
+    CK_TRY(attention_dispatch(a, st));
+    CK_TRY(lin(m, P(lay.att), BL, D, D, w.out, D, CK_EPI_RESID, P(lay.lat), D, 0, P(lay.lat), D,
+               st));
+    CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_mlp_w, w.norm_mlp_b, kLnEps,
+                    CK_NORM_LAYER, P(lay.x), D, st));
+    CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, m->mlp_hidden, CK_EPI_GELU, nullptr, 0, 0,
+               P(lay.hbuf), m->mlp_hidden, st));
+    CK_TRY(lin(m, P(lay.hbuf), BL, m->mlp_hidden, m->mlp_hidden, w.mlp2, D, CK_EPI_RESID,
+               P(lay.lat), D, 0, P(lay.lat), D, st));
+  }
+  // 8. final_norm then the head's norm
+  CK_TRY(row_norm2(P(lay.lat), m->dtype, BL, (int32_t)D, D, m->final_norm_w, m->final_norm_b,
+                   m->head_norm_w, m->head_norm_b, kLnEps, P(lay.x), D, st));
+  // 9. behaviour head
+  CK_TRY(lin(m, m->head_query, nq, D, D, m->head_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qh), D,
+             st));
+  CK_TRY(lin(m, P(lay.x), BL, D, D, m->head_kv, 2 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
+             2 * D, st));
+  {
+    ck_attention_args a = attn_base(m);
+    a.B = B;
+    a.H = (int32_t)H;
+    a.Dh = (int32_t)Dh;
+    a.Lq = (int32_t)nq;
+    a.n_keys = (int32_t)L;
+    a.q = P(lay.qh);
+    a.q_ld = D;
+    a.q_rows = nq;
+    a.q_col_per_h = Dh;
+    a.k = P(lay.qkv);
+    a.k_ld = 2 * D;
+    a.k_rows = BL;
+    a.k_rows_per_b = L;
+    a.k_col_per_h = Dh;
+    a.v = reinterpret_cast<uint8_t*>(P(lay.qkv)) + D * es_b;
+    a.v_ld = 2 * D;
+    a.v_rows = BL;
+    a.v_rows_per_b = L;
+    a.v_col_per_h = Dh;
+    a.o = P(lay.oh);
+    a.o_ld = D;
+    a.o_rows_per_b = nq;
+    a.o_col_per_h = Dh;
+    a.scale = 1.0f / sqrtf((float)Dh);
+    CK_TRY(attention_dispatch(a, st));
+  }
+  CK_TRY(lin(m, P(lay.oh), (int64_t)B * nq, D, D, m->head_out, 1, CK_EPI_STORE, nullptr, 0, 0,
+             out, 1, st));
+#undef CK_TRY
+  return CK_OK;
+}

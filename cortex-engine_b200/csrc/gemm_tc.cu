@@ -1,0 +1,442 @@
+// tcgen05 GEMM for the Cortex linears on B200 (sm_100a).
+//
+//   Y[M, N] = epilogue( A[M, K] (bf16, K-major) x B^T )
+//
+// B is the weight: (N, K) bf16 K-major (nn.Linear), (K, N) bf16 N-major
+// (rms_norm_linear's w), or (N, K) int8 K-major with per-output-channel fp32
+// scales (QuantizedLinear, cortex/quantization/calibrate.py:170-228). The int8
+// tile is widened to bf16 in shared memory by a converter warpgroup (exact for
+// |w| <= 127) and the scale is applied to the fp32 accumulator.
+//
+// Structure (one persistent CTA per SM, warp-specialised):
+//   warp 0      TMA producer: A and B tiles into a STAGES-deep smem ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, epilogue op,
+//               bf16 store (128 threads = the 128 TMEM lanes of the tile)
+//   warps 6..9  (int8 only) int8 -> bf16 converter
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the main loop of tile i+1. All mbarrier waits are bounded
+// (common.cuh); a timeout raises a CTA-wide abort flag and every role drains.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ck {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
+
+enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
+
+template <int BN, int WMODE>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;                        // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
+  static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
+  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
+  static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
+  static constexpr int NUM_THREADS = (WMODE == W_I8_NK) ? 320 : 192;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int num_m_tiles, num_n_tiles, num_k_blocks;
+  __nv_bfloat16* Y;
+  int64_t ldy;
+  const __nv_bfloat16* aux;
+  int64_t ld_aux;
+  int64_t aux_row_mod;
+  const float* w_scale;
+};
+
+__device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int m, int n0, const float* v,
+                                                int epi) {
+  // v: 32 fp32 accumulators for columns n0 .. n0+31 of row m.
+  float out[32];
+  const bool full = (n0 + 32 <= p.N);
+  float scale[32];
+  if (p.w_scale != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) scale[i] = (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float a = v[i];
+    if (p.w_scale != nullptr) a *= scale[i];
+    out[i] = rbf(a);  // linear output in bf16, as F.linear returns it
+  }
+  if (epi == CK_EPI_GELU) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) out[i] = gelu_erf(out[i]);
+  } else if (epi == CK_EPI_RESID || epi == CK_EPI_BIAS) {
+    const __nv_bfloat16* src;
+    if (epi == CK_EPI_RESID) {
+      int64_t r = p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;
+      src = p.aux + r * p.ld_aux + n0;
+    } else {
+      src = p.aux + n0;
+    }
+    if (full) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 raw = *reinterpret_cast<const uint4*>(src + 8 * c);
+        float f[8];
+        unpack8(raw, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[8 * c + j] = f[j] + out[8 * c + j];
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < p.N) out[i] = bf2f(src[i]) + out[i];
+    }
+  }
+  __nv_bfloat16* dst = p.Y + (int64_t)m * p.ldy + n0;
+  if (full) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(dst + 8 * c) = pack8(out + 8 * c);
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < p.N) dst[i] = f2bf(out[i]);
+  }
+}
+
+template <int BN, int WMODE, int EPI>
+__global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs p) {
+  using C = GemmCfg<BN, WMODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + C::STAGES * C::A_BYTES;
+  uint8_t* sB8 = sB + C::STAGES * C::B_BYTES;
+  uint8_t* sBar = sB8 + C::STAGES * C::B8_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* conv = empty + C::STAGES;
+  uint64_t* tfull = conv + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ── TMA producer ──
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const int mt = tile % p.num_m_tiles;
+        const int nt = tile / p.num_m_tiles;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 1)) break;
+          mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
+          if (WMODE == W_BF16_NK) {
+            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+          } else if (WMODE == W_BF16_KN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + stage * C::B_BYTES + j * (64 * BK * 2), &tmB, &full[stage],
+                          nt * BN + j * 64, kb * BK);
+          } else {
+            tma_load_2d(sB8 + stage * C::B8_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+          }
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: make sure every issued copy has landed before the CTA can exit.
+      for (int s = 0; s < C::STAGES && s < issued; ++s) {
+        int last = issued - 1 - ((issued - 1 - s) % C::STAGES);  // last load index into stage s
+        uint32_t par = (uint32_t)((last / C::STAGES) & 1);
+        mbar_wait(&full[s], par, nullptr, 9);
+      }
+    }
+  } else if (warp == 1) {
+    // ── MMA issuer ──
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          uint64_t* ready = (WMODE == W_I8_NK) ? &conv[stage] : &full[stage];
+          if (!mbar_wait(ready, phase, abort_flag, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t adesc = sw128_desc(a_addr + k * 32, 16, 1024);
+            uint64_t bdesc = (WMODE == W_BF16_KN)
+                                 ? sw128_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
+                                 : sw128_desc(b_addr + k * 32, 16, 1024);
+            tc_mma_ss(d_tmem, adesc, bdesc, C::IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // Drain all issued MMAs before TMEM / smem can be released.
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 8);
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ── epilogue ──
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mt = tile % p.num_m_tiles;
+      const int nt = tile / p.num_m_tiles;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
+      tc_fence_after();
+      const int m = mt * BM + row;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = nt * BN + c * 32;
+        float v[32];
+        tmem_ld32(tbase + (uint32_t)(c * 32), v);
+        tc_wait_ld();
+        if (m < p.M && n0 < p.N) store_row_chunk(p, m, n0, v, EPI);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  } else if (WMODE == W_I8_NK) {
+    // ── int8 -> bf16 converter (warps 6..9) ──
+    const int t = threadIdx.x - 192;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, 5)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = sB8 + stage * C::B8_BYTES;
+        uint8_t* dst = sB + stage * C::B_BYTES;
+        for (int i = t; i < BN * 4; i += 128) {
+          const int n = i >> 2;
+          const int c = i & 3;  // 16 int8 along K: k = 16c .. 16c+15
+          const int4 raw = *reinterpret_cast<const int4*>(src + n * 64 + c * 16);
+          const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+          float f[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) f[j] = (float)b[j];
+          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c)) = pack8(f);
+          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c + 1)) = pack8(f + 8);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[stage]);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ── host side ────────────────────────────────────────────────────────────────
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+}  // namespace
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                  uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t box_inner,
+                  uint32_t box_outer, bool swizzle128) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+namespace {
+
+template <int BN, int WMODE, int EPI>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                cudaStream_t st) {
+  using C = GemmCfg<BN, WMODE>;
+  auto kern = gemm_tc_kernel<BN, WMODE, EPI>;
+  if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
+    return record_cuda_error();
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  return check_launch();
+}
+
+template <int BN, int WMODE>
+int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                 cudaStream_t st) {
+  switch (epi) {
+    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE>(ta, tb, a, st);
+    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU>(ta, tb, a, st);
+    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID>(ta, tb, a, st);
+    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS>(ta, tb, a, st);
+  }
+  return CK_ERR_INVALID_ARG;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_layout, int64_t N,
+                       int64_t ldw, const void* A, const void* W, int64_t ldy, const void* Y,
+                       int epi, const void* aux, int64_t ld_aux) {
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  if (!al16(A) || !al16(W) || !al16(Y)) return false;
+  if ((lda * 2) % 16 != 0 || (ldy * 2) % 16 != 0) return false;
+  if (w_dtype == CK_I8) {
+    if (w_layout != CK_W_NK || ldw % 16 != 0) return false;
+  } else if (w_dtype == CK_BF16) {
+    if ((ldw * 2) % 16 != 0) return false;
+  } else {
+    return false;
+  }
+  if (epi == CK_EPI_RESID || epi == CK_EPI_BIAS) {
+    if (!al16(aux)) return false;
+    if (epi == CK_EPI_RESID && (ld_aux * 2) % 16 != 0) return false;
+  }
+  return true;
+}
+
+int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
+            int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
+            int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st) {
+  const int BN = (N % 256 == 0 || N > 256) ? 256 : 128;
+  GemmArgs a;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.num_m_tiles = (int)((M + BM - 1) / BM);
+  a.num_n_tiles = (int)((N + BN - 1) / BN);
+  a.num_k_blocks = (int)((K + BK - 1) / BK);
+  a.Y = reinterpret_cast<__nv_bfloat16*>(Y);
+  a.ldy = ldy;
+  a.aux = reinterpret_cast<const __nv_bfloat16*>(aux);
+  a.ld_aux = ld_aux;
+  a.aux_row_mod = aux_row_mod;
+  a.w_scale = (w_dtype == CK_I8) ? w_scale : nullptr;
+  if (w_dtype == CK_I8 && w_scale == nullptr) return CK_ERR_INVALID_ARG;
+
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, true))
+    return CK_ERR_INVALID_ARG;
+  bool ok;
+  if (w_dtype == CK_I8) {
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldw, BK, BN, false);
+  } else if (w_layout == CK_W_NK) {
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, ldw, BK, BN, true);
+  } else {
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, 64, BK, true);
+  }
+  if (!ok) return CK_ERR_INVALID_ARG;
+
+  if (BN == 256) {
+    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, ta, tb, a, st);
+    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, ta, tb, a, st);
+    return dispatch_epi<256, W_BF16_KN>(epi, ta, tb, a, st);
+  }
+  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, ta, tb, a, st);
+  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, ta, tb, a, st);
+  return dispatch_epi<128, W_BF16_KN>(epi, ta, tb, a, st);
+}
+
+}  // namespace ck

@@ -1,0 +1,215 @@
+// Fused spike tokenizer (cortex/kernels/tokenizer.py:68-81 and :177-249;
+// cortex/models/tokenizer.py:90-93):
+//
+//   out[dest[e], :] = n_emb[nid[e], :] + t_emb[tb[e], :] + v_emb[val[e], :]
+//
+// evaluated left to right in the table dtype, so bf16 tables give
+// bf16(bf16(n + t) + v) exactly as torch eager does. One warp per event; each
+// lane moves 16-byte vectors of the three rows (D = 512 bf16: 2 vectors per
+// lane per table). With gamma != NULL the finished row is LayerNorm-ed in
+// registers before the store, which fuses CrossAttentionBlock.norm_kv
+// (cortex/models/perceiver.py:68) into the gather: the raw tokens never reach HBM.
+// Out-of-range indices set CK_ERR_INDEX and write a zero row.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ck {
+
+namespace {
+
+__device__ __forceinline__ int64_t load_idx(const void* p, int dt, int64_t i, int64_t stride) {
+  if (dt == CK_I64) return reinterpret_cast<const int64_t*>(p)[i * stride];
+  return (int64_t) reinterpret_cast<const int32_t*>(p)[i * stride];
+}
+
+template <typename T>
+struct Vec;
+template <>
+struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ static void load(const __nv_bfloat16* p, float* f) {
+    unpack8(*reinterpret_cast<const uint4*>(p), f);
+  }
+  __device__ static void store(__nv_bfloat16* p, const float* f) {
+    *reinterpret_cast<uint4*>(p) = pack8(f);
+  }
+  __device__ static float round(float x) { return rbf(x); }
+};
+template <>
+struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, float* f) {
+    float4 v = *reinterpret_cast<const float4*>(p);
+    f[0] = v.x;
+    f[1] = v.y;
+    f[2] = v.z;
+    f[3] = v.w;
+  }
+  __device__ static void store(float* p, const float* f) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+  __device__ static float round(float x) { return x; }
+};
+
+struct TokArgs {
+  const void *n_emb, *t_emb, *v_emb;
+  int64_t n_vocab, t_vocab, v_vocab, n_ld, t_ld, v_ld;
+  const void *nid, *tb, *val;
+  int idx_dt;
+  int64_t s_nid, s_tb, s_val, E;
+  const int32_t* dest;
+  const void *gamma, *beta;
+  float eps;
+  void* out;
+  int64_t out_ld;
+  int D;
+};
+
+// VEC: elements per vector access (Vec<T>::N, or 1 for unaligned shapes).
+// MAXV: vectors per lane kept in registers (LayerNorm needs the whole row).
+template <typename T, int VEC, int MAXV, bool LN>
+__global__ void tokenize_kernel(const TokArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const T* ne = reinterpret_cast<const T*>(a.n_emb);
+  const T* te = reinterpret_cast<const T*>(a.t_emb);
+  const T* ve = reinterpret_cast<const T*>(a.v_emb);
+  T* out = reinterpret_cast<T*>(a.out);
+  const int nvec = a.D / VEC;
+  for (int64_t e = warp; e < a.E; e += nwarps) {
+    const int64_t dst_row = a.dest ? (int64_t)a.dest[e] : e;
+    if (dst_row < 0) continue;
+    const int64_t n = load_idx(a.nid, a.idx_dt, e, a.s_nid);
+    const int64_t t = load_idx(a.tb, a.idx_dt, e, a.s_tb);
+    const int64_t v = load_idx(a.val, a.idx_dt, e, a.s_val);
+    const bool ok = n >= 0 && n < a.n_vocab && t >= 0 && t < a.t_vocab && v >= 0 && v < a.v_vocab;
+    if (!ok && lane == 0) set_status(CK_ERR_INDEX, (int)e, (int)(n < 0 || n >= a.n_vocab ? n : (t < 0 || t >= a.t_vocab ? t : v)));
+    float x[MAXV][VEC];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        if (ok) {
+          float fn[VEC], ft[VEC], fv[VEC];
+          if constexpr (VEC == 1) {
+            fn[0] = (float)ne[n * a.n_ld + c];
+            ft[0] = (float)te[t * a.t_ld + c];
+            fv[0] = (float)ve[v * a.v_ld + c];
+          } else {
+            Vec<T>::load(ne + n * a.n_ld + c * VEC, fn);
+            Vec<T>::load(te + t * a.t_ld + c * VEC, ft);
+            Vec<T>::load(ve + v * a.v_ld + c * VEC, fv);
+          }
+#pragma unroll
+          for (int k = 0; k < VEC; ++k)
+            x[i][k] = Vec<T>::round(Vec<T>::round(fn[k] + ft[k]) + fv[k]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) x[i][k] = 0.f;
+        }
+      }
+    }
+    if (LN && ok) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+        if (lane + 32 * i < nvec)
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) s += x[i][k];
+      const float mean = warp_sum(s) / (float)a.D;
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+        if (lane + 32 * i < nvec)
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) {
+            const float d = x[i][k] - mean;
+            q += d * d;
+          }
+      const float var = warp_sum(q) / (float)a.D;
+      const float rstd = 1.0f / sqrtf(var + a.eps);
+      const T* g = reinterpret_cast<const T*>(a.gamma);
+      const T* bt = reinterpret_cast<const T*>(a.beta);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) {
+            const float gk = (float)g[c * VEC + k];
+            const float bk = bt ? (float)bt[c * VEC + k] : 0.f;
+            x[i][k] = (x[i][k] - mean) * rstd * gk + bk;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        if constexpr (VEC == 1) {
+          out[dst_row * a.out_ld + c] = (T)x[i][0];
+        } else {
+          Vec<T>::store(out + dst_row * a.out_ld + c * VEC, x[i]);
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int VEC, int MAXV, bool LN>
+int launch_tok(const TokArgs& a, cudaStream_t st) {
+  int64_t blocks = (a.E * 32 + 255) / 256;
+  const int cap = 32 * num_sms();
+  if (blocks > cap) blocks = cap;
+  tokenize_kernel<T, VEC, MAXV, LN><<<(unsigned)blocks, 256, 0, st>>>(a);
+  return check_launch();
+}
+
+template <typename T>
+int dispatch_tok(const TokArgs& a, bool vec_ok, cudaStream_t st) {
+  constexpr int V = Vec<T>::N;
+  const bool ln = a.gamma != nullptr;
+  if (vec_ok) {
+    const int per_lane = (a.D / V + 31) / 32;
+    if (per_lane <= 2) return ln ? launch_tok<T, V, 2, true>(a, st) : launch_tok<T, V, 2, false>(a, st);
+    if (per_lane <= 4) return ln ? launch_tok<T, V, 4, true>(a, st) : launch_tok<T, V, 4, false>(a, st);
+    if (per_lane <= 8) return ln ? launch_tok<T, V, 8, true>(a, st) : launch_tok<T, V, 8, false>(a, st);
+    if (!ln) {
+      // long rows without a norm: process in register-sized column slices
+      return CK_ERR_UNSUPPORTED;
+    }
+    return CK_ERR_UNSUPPORTED;
+  }
+  const int per_lane = (a.D + 31) / 32;
+  if (per_lane <= 8) return ln ? launch_tok<T, 1, 8, true>(a, st) : launch_tok<T, 1, 8, false>(a, st);
+  if (per_lane <= 32) return ln ? launch_tok<T, 1, 32, true>(a, st) : launch_tok<T, 1, 32, false>(a, st);
+  return CK_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype, int32_t D,
+             int64_t n_vocab, int64_t t_vocab, int64_t v_vocab, int64_t n_ld, int64_t t_ld,
+             int64_t v_ld, const void* nid, const void* tb, const void* val, int idx_dtype,
+             int64_t s_nid, int64_t s_tb, int64_t s_val, int64_t E, const int32_t* dest,
+             const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
+             cudaStream_t st) {
+  if (E == 0) return CK_OK;
+  if (E < 0 || D <= 0 || !n_emb || !t_emb || !v_emb || !nid || !tb || !val || !out)
+    return CK_ERR_INVALID_ARG;
+  if (idx_dtype != CK_I64 && idx_dtype != CK_I32) return CK_ERR_UNSUPPORTED;
+  TokArgs a{n_emb, t_emb, v_emb, n_vocab, t_vocab, v_vocab, n_ld, t_ld, v_ld, nid, tb, val,
+            idx_dtype, s_nid, s_tb, s_val, E, dest, gamma, beta, eps, out, out_ld, D};
+  const int es = dtype == CK_F32 ? 4 : 2;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec_ok = ((int64_t)D * es) % 16 == 0 && (n_ld * es) % 16 == 0 &&
+                      (t_ld * es) % 16 == 0 && (v_ld * es) % 16 == 0 && (out_ld * es) % 16 == 0 &&
+                      al16(n_emb) && al16(t_emb) && al16(v_emb) && al16(out);
+  if (dtype == CK_BF16) return dispatch_tok<__nv_bfloat16>(a, vec_ok, st);
+  if (dtype == CK_F32) return dispatch_tok<float>(a, vec_ok, st);
+  return CK_ERR_UNSUPPORTED;
+}
+
+}  // namespace ck

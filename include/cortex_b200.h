@@ -1,0 +1,208 @@
+/*
+ * cortex_b200.h — C ABI of the B200 (sm_100a) Cortex decoder forward hot path.
+ *
+ * Every entry point takes raw device pointers, element strides and an explicit
+ * cudaStream_t (passed as void*), allocates nothing, and returns an int status
+ * (CK_OK = 0, negative on error). Kernels that find bad data on the device
+ * (an index out of range, a bounded wait that gave up) record a code in a
+ * per-device status word that ck_get_last_status() reads back.
+ *
+ * The entry points replace the reference (peterajhgraham/cortex-engine) call
+ * sites cited beside each one; the Python package in cortex-engine_b200/cortex
+ * binds them with ctypes behind the reference's unchanged Python signatures.
+ */
+#ifndef CORTEX_B200_H_
+#define CORTEX_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── status codes ─────────────────────────────────────────────────────────── */
+#define CK_OK 0
+#define CK_ERR_INVALID_ARG -1 /* bad shape, stride, alignment or pointer */
+#define CK_ERR_UNSUPPORTED -2 /* dtype / layout combination not built */
+#define CK_ERR_CUDA -3        /* a CUDA runtime call failed (see ck_last_cuda_error) */
+#define CK_ERR_INDEX -4       /* device: an event index is outside its table / batch */
+#define CK_ERR_TIMEOUT -5     /* device: a bounded pipeline wait gave up */
+#define CK_ERR_WORKSPACE -6   /* workspace smaller than the *_workspace_bytes query */
+
+/* ── element types ────────────────────────────────────────────────────────── */
+#define CK_F32 0
+#define CK_BF16 1
+#define CK_I8 2
+#define CK_I32 3
+#define CK_I64 4
+
+/* ── norm modes and GEMM epilogues ────────────────────────────────────────── */
+#define CK_NORM_NONE 0
+#define CK_NORM_LAYER 1 /* (x - mean) * rstd * gamma + beta (nn.LayerNorm) */
+#define CK_NORM_RMS 2   /* x / sqrt(mean(x^2) + eps) * gamma              */
+
+#define CK_EPI_STORE 0 /* y = dtype(acc)                                  */
+#define CK_EPI_GELU 1  /* y = dtype(gelu_erf(dtype(acc)))                 */
+#define CK_EPI_RESID 2 /* y = dtype(aux[m % mod] + dtype(acc))            */
+#define CK_EPI_BIAS 3  /* y = dtype(dtype(acc) + aux[n])                  */
+
+#define CK_W_NK 0 /* weight stored (N, K): nn.Linear / QuantizedLinear */
+#define CK_W_KN 1 /* weight stored (K, N): rms_norm_linear's w        */
+
+/* Status word of the current device. Synchronises the device, copies the word
+ * (and 4 info ints, may be NULL) out and clears it. Returns the code. */
+int ck_get_last_status(int* info4);
+/* Last CUDA runtime error recorded by an entry point that returned CK_ERR_CUDA. */
+int ck_last_cuda_error(void);
+const char* ck_status_string(int code);
+/* Number of SMs of the current device (0 if none). */
+int ck_num_sms(void);
+/* Kernel launches issued by this library since it was loaded (all threads). */
+long long ck_launch_count(void);
+
+/* ── 1. event packing ───────────────────────────────────────────────────────
+ * Replaces _pack_events' index work (cortex/models/cortex.py:125-165):
+ * bincount (:141), E_max (:142), stable argsort (:149), exclusive cumsum (:155-160),
+ * pos_within (:161). Outputs counts[B], offsets[B+1] (offsets[B] = E),
+ * dest[E] (packed row of every input event = offsets[b] + pos_within) and
+ * e_max[1]. B must equal max(batch_indices)+1 (the reference's :140); an index
+ * outside [0, B) sets CK_ERR_INDEX. */
+size_t ck_pack_workspace_bytes(int64_t E, int32_t B);
+int ck_pack_events(const void* batch_indices, int idx_dtype, int64_t idx_stride, int64_t E,
+                   int32_t B, int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* e_max,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Padded layout of _pack_events (cortex/models/cortex.py:146-165): out[b, pos, :]
+ * = flat[e, :], mask[b, pos] = 1, with pos = dest[e] - offsets[b]. `out` and
+ * `mask` must be zeroed by the caller, as the reference's torch.zeros are. */
+int ck_pack_scatter(const void* flat, int dtype, int64_t E, int32_t D, int64_t flat_stride,
+                    const void* batch_indices, int idx_dtype, int64_t idx_stride,
+                    const int32_t* dest, const int32_t* offsets, int32_t e_max, void* out,
+                    uint8_t* mask, void* stream);
+
+/* ── 2. tokenizer ───────────────────────────────────────────────────────────
+ * Replaces fused_tokenizer (cortex/kernels/tokenizer.py:177-249) and the eager
+ * sum of SpikeTokenizer.forward (cortex/models/tokenizer.py:90-93):
+ * out[dest[e]] = n_emb[nid[e]] + t_emb[tb[e]] + v_emb[val[e]], left to right in
+ * the table dtype. dest may be NULL (identity). With gamma != NULL the row is
+ * then LayerNorm-ed (eps, gamma, beta) before it is stored (fuses
+ * CrossAttentionBlock.norm_kv, cortex/models/perceiver.py:68). */
+int ck_tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype, int32_t D,
+                int64_t n_vocab, int64_t t_vocab, int64_t v_vocab, int64_t n_ld, int64_t t_ld,
+                int64_t v_ld, const void* nid, const void* tb, const void* val, int idx_dtype,
+                int64_t s_nid, int64_t s_tb, int64_t s_val, int64_t E, const int32_t* dest,
+                const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
+                void* stream);
+
+/* ── 3. row norm ────────────────────────────────────────────────────────────
+ * nn.LayerNorm (cortex/models/perceiver.py:51-52,97-98,143) or the RMSNorm of
+ * rms_norm_linear_reference (cortex/kernels/fused_rmsnorm.py:86-108), fp32
+ * statistics, output rounded to dtype. */
+int ck_row_norm(const void* x, int dtype, int64_t M, int32_t D, int64_t ldx, const void* gamma,
+                const void* beta, float eps, int mode, void* y, int64_t ldy, void* stream);
+
+/* ── 4. linear ──────────────────────────────────────────────────────────────
+ * y = epi(A @ W^T) for W (N,K) [nn.Linear, QuantizedLinear: cortex/quantization/
+ * calibrate.py:225-228] or y = epi(A @ W) for W (K,N) [rms_norm_linear's w,
+ * cortex/kernels/fused_rmsnorm.py:239]. W may be int8 with per-output-channel
+ * fp32 scales (w_scale[N]); it is widened to bf16 inside the kernel and the
+ * scale applied to the fp32 accumulator. bf16 problems whose strides are
+ * 16-byte aligned run on the tcgen05 tensor-core kernel; fp32 problems (and
+ * unaligned bf16 ones) on an fp32-accumulating CUDA-core kernel. */
+int ck_linear(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
+              int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi,
+              const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy,
+              void* stream);
+
+/* Norm then linear: replaces rms_norm_linear (cortex/kernels/fused_rmsnorm.py:239-301)
+ * with norm_mode = CK_NORM_RMS, and LayerNorm->Linear pairs of the model with
+ * CK_NORM_LAYER. workspace must hold M*K elements of dtype. */
+size_t ck_norm_linear_workspace_bytes(int dtype, int64_t M, int64_t K);
+int ck_norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* gamma,
+                   const void* beta, float eps, int norm_mode, const void* W, int w_dtype,
+                   int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi,
+                   const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ── 5. attention ───────────────────────────────────────────────────────────
+ * softmax(q k^T * scale + mask) v per (batch b, head h), fp32 statistics.
+ * Row r of (b, h) for tensor X in {q, k, v, o} lives at
+ *   X + (b*X_rows_per_b + h*X_rows_per_h + r) * X_ld + h*X_col_per_h
+ * except that with key_offsets != NULL the k/v rows of batch b start at
+ * key_offsets[b] (packed varlen events, n_keys(b) = key_offsets[b+1]-key_offsets[b]).
+ * key_mask (uint8, may be NULL) drops key e of batch b when key_mask[b*key_mask_ld + e]
+ * is 0: the (B, 1, 1, E) bool attn_mask of cortex/models/perceiver.py:74-80.
+ * block_mask (n_q_tiles x n_k_tiles, uint8, may be NULL) skips (BLOCK_L x BLOCK_E)
+ * tiles as sparse_cross_attention does (cortex/kernels/sparse_xattn.py:340-434);
+ * a query row with no unmasked key returns 0 (the kernel's l = 0 guard, :326-328,
+ * and torch SDPA's fully-masked-row result on CPU). Replaces the SDPA calls of
+ * cortex/models/perceiver.py:80,121 and cortex/models/cortex.py:49. */
+typedef struct ck_attention_args {
+  int dtype;
+  int32_t B, H, Dh, Lq;
+  int32_t n_keys;
+  const int32_t* key_offsets;
+  const void* q;
+  int64_t q_ld, q_rows, q_rows_per_b, q_rows_per_h, q_col_per_h;
+  const void* k;
+  int64_t k_ld, k_rows, k_rows_per_b, k_rows_per_h, k_col_per_h;
+  const void* v;
+  int64_t v_ld, v_rows, v_rows_per_b, v_rows_per_h, v_col_per_h;
+  void* o;
+  int64_t o_ld, o_rows_per_b, o_rows_per_h, o_col_per_h;
+  const uint8_t* block_mask;
+  int32_t n_q_tiles, n_k_tiles, block_l, block_e;
+  const uint8_t* key_mask;
+  int64_t key_mask_ld;
+  float scale;
+} ck_attention_args;
+
+int ck_attention(const ck_attention_args* args, void* stream);
+
+/* ── 6. whole forward ───────────────────────────────────────────────────────
+ * CortexModel.forward (cortex/models/cortex.py:90-122) for return_aux=False:
+ * tokenizer + packing + Perceiver encoder + behaviour head, all on the device,
+ * no host synchronisation. Weights are the module's parameters in place
+ * (bf16 or fp32); QuantizedLinear layers pass int8 weights and fp32 scales. */
+typedef struct ck_linear_weight {
+  const void* w;       /* (N, K) */
+  int dtype;           /* CK_BF16, CK_F32 or CK_I8 */
+  const float* scale;  /* (N,) for CK_I8, else NULL */
+  const void* bias;    /* (N,) or NULL */
+} ck_linear_weight;
+
+typedef struct ck_block_weights {
+  const void *norm_attn_w, *norm_attn_b;
+  ck_linear_weight qkv, out;
+  const void *norm_mlp_w, *norm_mlp_b;
+  ck_linear_weight mlp0, mlp2;
+} ck_block_weights;
+
+typedef struct ck_model {
+  int dtype; /* CK_BF16 or CK_F32: activations and float parameters */
+  int32_t hidden_dim, latent_dim, num_latents, num_layers, num_heads, head_dim;
+  int32_t cross_heads, mlp_hidden, behavior_dim;
+  int64_t n_vocab, t_vocab, v_vocab;
+  const void *neuron_emb, *time_emb, *value_emb;
+  const void* latents;
+  const void *norm_q_w, *norm_q_b, *norm_kv_w, *norm_kv_b;
+  ck_linear_weight cross_q, cross_kv, cross_out;
+  const ck_block_weights* blocks; /* host array of num_layers entries */
+  const void *final_norm_w, *final_norm_b;
+  const void* head_query; /* (behavior_dim, latent_dim) */
+  const void *head_norm_w, *head_norm_b;
+  ck_linear_weight head_q, head_kv, head_out;
+} ck_model;
+
+size_t ck_forward_workspace_bytes(const ck_model* m, int64_t E, int32_t B);
+int ck_forward(const ck_model* m, const void* neuron_ids, const void* time_bins,
+               const void* values, const void* batch_indices, int idx_dtype, int64_t E,
+               int32_t B, void* behavior_out, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CORTEX_B200_H_ */

@@ -1,0 +1,374 @@
+"""Kernel parity on the GPU, through the C ABI, against the CPU oracle.
+
+Shapes and tolerances follow the reference's own kernel tests
+(tests/unit/test_kernel_tokenizer.py, test_kernel_sparse_xattn.py,
+test_kernel_fused_rmsnorm.py): tokens bit-exact (fp32 and bf16), packing
+bit-exact, attention bf16 1e-2 / fp32 1e-4, RMSNorm+linear bf16 (1e-2, 1e-1)
+/ fp32 1e-4.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cortex_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _status_ok():
+    from cortex import _lib
+
+    code, info = _lib.device_status()
+    assert code == 0, (code, info)
+
+
+# ── packing ──────────────────────────────────────────────────────────────────
+
+
+def _check_pack(bidx_cpu: torch.Tensor, dtype=torch.int64):
+    from cortex.kernels import _ops
+
+    info = O.pack_events_index(bidx_cpu.numpy())
+    B = info["B"]
+    bidx = bidx_cpu.to(DEV, dtype)
+    counts, offsets, dest, e_max = _ops.pack_events(bidx, B)
+    torch.cuda.synchronize()
+    assert np.array_equal(counts.cpu().numpy(), info["counts"])
+    assert np.array_equal(offsets.cpu().numpy(), info["offsets"])
+    assert np.array_equal(dest.cpu().numpy(), info["dest"])
+    assert int(e_max.item()) == info["E_max"]
+    _status_ok()
+
+
+def test_pack_golden_cases(golden_kernels):
+    from cortex.models.cortex import _pack_events
+
+    for name, case in golden_kernels["pack"].items():
+        _check_pack(case["batch_indices"])
+        _check_pack(case["batch_indices"], torch.int32)
+        flat = (torch.arange(case["batch_indices"].shape[0], dtype=torch.float32)[:, None]
+                + 1.0).to(DEV)
+        tokens, mask = _pack_events(flat, case["batch_indices"].to(DEV))
+        assert torch.equal(tokens[..., 0].cpu().double(), case["tokens"]), name
+        assert torch.equal(mask.cpu(), case["mask"]), name
+
+
+@pytest.mark.parametrize("E,B,sort", [(16384, 32, True), (214_000, 256, True),
+                                      (50_000, 300, False), (1, 1, True), (4097, 7, False)])
+def test_pack_random(E, B, sort):
+    g = torch.Generator().manual_seed(E)
+    b = torch.randint(0, B, (E,), generator=g)
+    b[0] = B - 1
+    if sort:
+        b = b.sort().values
+    _check_pack(b)
+
+
+def test_pack_out_of_range_index_sets_status():
+    from cortex import _lib
+    from cortex.kernels import _ops
+
+    b = torch.tensor([0, 1, 5, 1], device=DEV)
+    _ops.pack_events(b, 2)
+    code, _ = _lib.device_status()
+    assert code == _lib.CK_ERR_INDEX
+
+
+# ── tokenizer ────────────────────────────────────────────────────────────────
+
+
+def _embs(N, T, V, D, dtype):
+    torch.manual_seed(42)
+    return (torch.randn(N, D, dtype=dtype), torch.randn(T, D, dtype=dtype),
+            torch.randn(V, D, dtype=dtype))
+
+
+def _ids(E, N, T, V):
+    torch.manual_seed(99)
+    return (torch.randint(0, N, (E,)), torch.randint(0, T, (E,)), torch.randint(0, V, (E,)))
+
+
+@pytest.mark.parametrize("E,D,N,T,V", [(1, 64, 32, 64, 8), (127, 64, 32, 64, 8),
+                                       (128, 64, 256, 512, 8), (1024, 128, 256, 512, 8),
+                                       (4096, 256, 512, 1024, 8), (16384, 512, 512, 1024, 16),
+                                       (100, 70, 16, 16, 4), (333, 768, 512, 1024, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tokenizer_bit_exact(E, D, N, T, V, dtype):
+    from cortex.kernels.tokenizer import fused_tokenizer
+
+    n, t, v = _embs(N, T, V, D, dtype)
+    nid, tb, val = _ids(E, N, T, V)
+    ref = O.tokenize(n, t, v, nid, tb, val)
+    out = fused_tokenizer(n.to(DEV), t.to(DEV), v.to(DEV), nid.to(DEV), tb.to(DEV), val.to(DEV))
+    assert out.shape == (E, D) and out.dtype == dtype
+    assert torch.equal(out.cpu(), ref)
+    _status_ok()
+
+
+def test_tokenizer_golden(golden_kernels):
+    from cortex.kernels.tokenizer import fused_tokenizer
+
+    for key, c in golden_kernels["tokenizer"].items():
+        out = fused_tokenizer(*(c[k].to(DEV) for k in ("n", "t", "v", "nid", "tb", "val")))
+        assert torch.equal(out.cpu(), c["out"]), key
+
+
+def test_tokenizer_empty_noncontiguous_int32():
+    from cortex.kernels.tokenizer import fused_tokenizer
+
+    n, t, v = (x.to(DEV) for x in _embs(32, 64, 8, 128, torch.float32))
+    e = torch.zeros(0, dtype=torch.int64, device=DEV)
+    assert fused_tokenizer(n, t, v, e, e, e).shape == (0, 128)
+    big = torch.randint(0, 32, (128,), device=DEV)
+    nid = big[::2]
+    tb = torch.randint(0, 64, (64,), device=DEV)
+    val = torch.randint(0, 8, (64,), device=DEV)
+    ref = O.tokenize(n.cpu(), t.cpu(), v.cpu(), nid.cpu(), tb.cpu(), val.cpu())
+    assert torch.equal(fused_tokenizer(n, t, v, nid, tb, val).cpu(), ref)
+    out32 = fused_tokenizer(n, t, v, nid.int(), tb.int(), val.int())
+    assert torch.equal(out32.cpu(), ref)
+
+
+def test_tokenizer_out_of_range_sets_status():
+    from cortex import _lib
+    from cortex.kernels.tokenizer import fused_tokenizer
+
+    n, t, v = (x.to(DEV) for x in _embs(8, 8, 4, 64, torch.float32))
+    idx = torch.tensor([0, 9], device=DEV)
+    fused_tokenizer(n, t, v, idx, torch.zeros_like(idx), torch.zeros_like(idx))
+    with pytest.raises(IndexError):
+        _lib.check_device_status("tokenizer")
+
+
+def test_tokenizer_with_fused_layernorm():
+    from cortex import _lib
+    from cortex.kernels import _ops
+
+    n, t, v = _embs(512, 1024, 8, 512, torch.bfloat16)
+    nid, tb, val = _ids(4096, 512, 1024, 8)
+    g = torch.rand(512, dtype=torch.bfloat16) + 0.5
+    b = torch.randn(512, dtype=torch.bfloat16) * 0.1
+    tok = O.tokenize(n, t, v, nid, tb, val)
+    ref = torch.nn.functional.layer_norm(tok, (512,), g, b, 1e-5).float()
+    out = _ops.tokenize(n.to(DEV), t.to(DEV), v.to(DEV), nid.to(DEV), tb.to(DEV), val.to(DEV),
+                        gamma=g.to(DEV), beta=b.to(DEV), eps=1e-5).float().cpu()
+    # one bf16 ulp where the fp32 statistics round differently
+    assert (out - ref).abs().max().item() <= 2 ** -6
+    assert (out != ref).float().mean().item() < 0.01
+    assert _lib.device_status()[0] == 0
+
+
+# ── row norm ─────────────────────────────────────────────────────────────────
+
+
+@pytest.mark.parametrize("M,D", [(8192, 512), (37, 256), (64, 768), (5, 70)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_layer_norm(M, D, dtype):
+    from cortex.kernels import _ops
+
+    torch.manual_seed(M + D)
+    x = torch.randn(M, D, dtype=dtype) * 3 + 0.5
+    g = (torch.rand(D) + 0.5).to(dtype)
+    b = (torch.randn(D) * 0.1).to(dtype)
+    ref = torch.nn.functional.layer_norm(x, (D,), g, b, 1e-5)
+    out = _ops.row_norm(x.to(DEV), g.to(DEV), b.to(DEV), 1e-5).cpu()
+    tol = dict(rtol=1e-5, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-2, atol=2e-2)
+    torch.testing.assert_close(out, ref, **tol)
+
+
+# ── linear / GEMM ────────────────────────────────────────────────────────────
+
+
+def _gemm_ref(x, w, w_scale=None, layout="nk"):
+    xf = x.float()
+    wf = w.float()
+    if layout == "kn":
+        wf = wf.t()
+    y = xf @ wf.t()
+    if w_scale is not None:
+        y = y * w_scale.float()[None, :]
+    return y
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 64, 128), (256, 512, 512), (8192, 512, 1536),
+                                   (8192, 512, 2048), (8192, 2048, 512), (33, 64, 97),
+                                   (300, 768, 2304), (2, 512, 512), (16384, 512, 1024)])
+def test_linear_tc_bf16(M, K, N):
+    from cortex.kernels import _ops
+
+    torch.manual_seed(M * 7 + N)
+    x = torch.randn(M, K, dtype=torch.bfloat16)
+    w = (torch.randn(N, K) / math.sqrt(K)).to(torch.bfloat16)
+    out = _ops.linear(x.to(DEV), w.to(DEV)).float().cpu()
+    ref = _gemm_ref(x, w)
+    rel = ((out - ref).norm() / ref.norm()).item()
+    assert rel < 5e-3, rel
+    assert (out - ref).abs().max().item() < 0.05 * ref.abs().max().item() + 1e-2
+    _status_ok()
+
+
+@pytest.mark.parametrize("M,K,N", [(8192, 512, 1536), (1000, 2048, 512), (64, 128, 256)])
+def test_linear_tc_int8(M, K, N):
+    from cortex.kernels import _ops
+
+    torch.manual_seed(N)
+    x = torch.randn(M, K, dtype=torch.bfloat16)
+    w = torch.randn(N, K) / math.sqrt(K)
+    w8, sc = O.quantize_weight(w)
+    out = _ops.linear(x.to(DEV), w8.to(DEV), w_scale=sc.to(DEV)).float().cpu()
+    ref = _gemm_ref(x, w8, sc)
+    rel = ((out - ref).norm() / ref.norm()).item()
+    assert rel < 5e-3, rel
+    # and against the reference formulation: dequantise to bf16, then F.linear
+    p = {"l.weight_int8": w8, "l.weight_scale": sc}
+    ref2 = O.linear(x, p, "l").float()
+    assert ((out - ref2).norm() / ref2.norm()).item() < 1e-2
+    _status_ok()
+
+
+@pytest.mark.parametrize("epi", ["gelu", "resid", "resid_mod", "bias"])
+def test_linear_epilogues(epi):
+    from cortex import _lib as L
+    from cortex.kernels import _ops
+
+    torch.manual_seed(3)
+    M, K, N = 1024, 512, 512
+    x = torch.randn(M, K, dtype=torch.bfloat16)
+    w = (torch.randn(N, K) / math.sqrt(K)).to(torch.bfloat16)
+    y = _gemm_ref(x, w).to(torch.bfloat16).float()
+    if epi == "gelu":
+        out = _ops.linear(x.to(DEV), w.to(DEV), epi=L.CK_EPI_GELU)
+        ref = torch.nn.functional.gelu(y)
+    elif epi == "resid":
+        r = torch.randn(M, N, dtype=torch.bfloat16)
+        out = _ops.linear(x.to(DEV), w.to(DEV), epi=L.CK_EPI_RESID, aux=r.to(DEV))
+        ref = r.float() + y
+    elif epi == "resid_mod":
+        r = torch.randn(256, N, dtype=torch.bfloat16)
+        out = _ops.linear(x.to(DEV), w.to(DEV), epi=L.CK_EPI_RESID, aux=r.to(DEV),
+                          aux_row_mod=256)
+        ref = r.float().repeat(M // 256, 1) + y
+    else:
+        bias = torch.randn(N, dtype=torch.bfloat16)
+        out = _ops.linear(x.to(DEV), w.to(DEV), epi=L.CK_EPI_BIAS, aux=bias.to(DEV))
+        ref = y + bias.float()
+    out = out.float().cpu()
+    rel = ((out - ref).norm() / ref.norm()).item()
+    assert rel < 1e-2, rel
+
+
+@pytest.mark.parametrize("M,K,N", [(16, 64, 128), (64, 128, 256), (256, 512, 512),
+                                   (8192, 512, 1536), (8192, 512, 2048), (33, 70, 97)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rms_norm_linear(M, K, N, dtype):
+    from cortex.kernels.fused_rmsnorm import rms_norm_linear
+
+    torch.manual_seed(17)
+    x = torch.randn(M, K, dtype=dtype)
+    gamma = torch.ones(K, dtype=dtype)
+    w = torch.randn(K, N, dtype=dtype)
+    out = rms_norm_linear(x.to(DEV), gamma.to(DEV), w.to(DEV))
+    assert out.shape == (M, N) and out.dtype == dtype
+    if dtype == torch.float32:
+        ref = O.rms_norm_linear(x, gamma, w, None)
+        torch.testing.assert_close(out.cpu(), ref, rtol=1e-4, atol=1e-4)
+    else:
+        # reference rounding points, fp32 accumulation of the bf16 product
+        xf = x.float()
+        xn = ((xf / torch.sqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)) * gamma.float())
+        ref = (xn.to(dtype).float() @ w.float()).to(dtype)
+        torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-1)
+
+
+def test_rms_norm_linear_bias_and_3d(golden_kernels):
+    from cortex.kernels.fused_rmsnorm import rms_norm_linear
+
+    c = golden_kernels["rmsnorm"]
+    out = rms_norm_linear(c["x"].to(DEV), c["gamma"].to(DEV), c["w"].to(DEV), c["bias"].to(DEV))
+    torch.testing.assert_close(out.cpu(), c["out_bias"], rtol=1e-4, atol=1e-4)
+    out = rms_norm_linear(c["x"].to(DEV), c["gamma2"].to(DEV), c["w"].to(DEV))
+    torch.testing.assert_close(out.cpu(), c["out_gamma2"], rtol=1e-4, atol=1e-4)
+    torch.manual_seed(0)
+    x = torch.randn(2, 256, 512)
+    w = torch.randn(512, 1536)
+    out = rms_norm_linear(x.to(DEV), torch.ones(512, device=DEV), w.to(DEV))
+    assert out.shape == (2, 256, 1536)
+    ref = O.rms_norm_linear(x.reshape(512, 512), torch.ones(512), w, None).reshape(2, 256, 1536)
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-4, atol=1e-4)
+
+
+# ── attention ────────────────────────────────────────────────────────────────
+
+
+def _qkv(B, H, L, E, Dh, dtype):
+    torch.manual_seed(123)
+    return (torch.randn(B, H, L, Dh, dtype=dtype), torch.randn(B, H, E, Dh, dtype=dtype),
+            torch.randn(B, H, E, Dh, dtype=dtype))
+
+
+@pytest.mark.parametrize("B,H,L,E,Dh", [(1, 1, 32, 64, 16), (2, 4, 64, 128, 32),
+                                        (1, 8, 128, 256, 64), (2, 8, 256, 512, 64),
+                                        (3, 2, 200, 77, 64), (1, 2, 130, 1000, 64)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_attention_dense(B, H, L, E, Dh, dtype):
+    from cortex.kernels.sparse_xattn import sparse_cross_attention
+
+    q, k, v = _qkv(B, H, L, E, Dh, dtype)
+    mask = torch.ones(math.ceil(L / 32), math.ceil(E / 32), dtype=torch.bool)
+    ref = O.sparse_cross_attention(q.float(), k.float(), v.float(), mask, 32, 32)
+    out = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask, 32, 32)
+    assert out.shape == q.shape and out.dtype == dtype
+    tol = (1e-2, 1e-2) if dtype == torch.bfloat16 else (1e-4, 1e-4)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=tol[0], atol=tol[1])
+    none = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), None)
+    torch.testing.assert_close(none.float().cpu(), ref, rtol=tol[0], atol=tol[1])
+    _status_ok()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("BL,BE", [(32, 32), (64, 64), (16, 128)])
+def test_attention_checkerboard(dtype, BL, BE):
+    from cortex.kernels.sparse_xattn import sparse_cross_attention
+
+    B, H, L, E, Dh = 2, 4, 256, 512, 64
+    q, k, v = _qkv(B, H, L, E, Dh, dtype)
+    n_q, n_k = math.ceil(L / BL), math.ceil(E / BE)
+    mask = torch.tensor([[(i + j) % 2 == 0 for j in range(n_k)] for i in range(n_q)])
+    ref = O.sparse_cross_attention(q.float(), k.float(), v.float(), mask, BL, BE)
+    out = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask, BL, BE)
+    tol = (1e-2, 1e-2) if dtype == torch.bfloat16 else (1e-4, 1e-4)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=tol[0], atol=tol[1])
+
+
+def test_attention_golden_and_all_masked(golden_kernels):
+    from cortex.kernels.sparse_xattn import sparse_cross_attention
+
+    c = golden_kernels["xattn"]
+    q, k, v = c["q"].to(DEV), c["k"].to(DEV), c["v"].to(DEV)
+    for key, m in (("dense", c["dense_mask"]), ("checker", c["checker_mask"])):
+        torch.testing.assert_close(sparse_cross_attention(q, k, v, m, 32, 32).cpu(), c[key],
+                                   rtol=1e-4, atol=1e-4)
+    for dtype in (torch.float32, torch.bfloat16):
+        q, k, v = _qkv(1, 2, 128, 256, 64, dtype)
+        z = torch.zeros(2, 4, dtype=torch.bool)
+        out = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), z, 64, 64)
+        assert torch.equal(out.cpu(), torch.zeros_like(q))
+
+
+def test_attention_temporal_mask():
+    from cortex.kernels.sparse_xattn import build_temporal_block_mask, sparse_cross_attention
+
+    B, H, L, E, Dh = 2, 8, 256, 512, 64
+    q, k, v = _qkv(B, H, L, E, Dh, torch.bfloat16)
+    et = torch.randint(0, 600, (E,), generator=torch.Generator().manual_seed(1)).sort().values
+    mask = build_temporal_block_mask(et, L, 600, 30, 64, 64)
+    assert 0 < mask.float().mean() < 1
+    ref = O.sparse_cross_attention(q.float(), k.float(), v.float(), mask, 64, 64)
+    out = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask, 64, 64)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=1e-2, atol=1e-2)

@@ -1,0 +1,135 @@
+"""End-to-end kinematics parity of CortexModel.forward on the GPU.
+
+Against the reference's own outputs (golden vectors) and the CPU oracle, with
+the north-star tolerances written here: norm-wise relative error
+||y - y_ref|| / ||y_ref|| <= 1e-4 for fp32 and <= 2e-2 for bf16 / INT8. Full-size
+batches are additionally checked through size-independent properties: every
+window's result is independent of the rest of the batch (bit-exact), and the
+packing is invariant to how the events of different windows are interleaved.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cortex_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = {"float32": 1e-4, "bfloat16": 2e-2}
+
+
+def _rel(y, ref):
+    y, ref = y.float().cpu(), ref.float().cpu()
+    return float((y - ref).norm() / ref.norm())
+
+
+def _model(name):
+    from cortex.workloads import WORKLOADS, build_model
+
+    wl = WORKLOADS[name]
+    return wl, build_model(wl, DEV)
+
+
+@pytest.mark.parametrize("name", ["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"])
+def test_forward_matches_reference_golden(golden_models, name):
+    from cortex import _lib
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    g = golden_models[name]
+    n = g["behavior"].shape[0]
+    inp, _ = make_inputs(wl, seed=0, batch=n)
+    with torch.no_grad():
+        y = model(*(inp[k].to(DEV) for k in ("neuron_ids", "time_bins", "values",
+                                            "batch_indices")))["behavior"]
+    assert y.shape == (n, wl.config.behavior_dim)
+    assert torch.isfinite(y).all()
+    rel = _rel(y, g["behavior"])
+    assert rel <= TOL[wl.dtype], rel
+    assert _lib.device_status()[0] == 0
+
+
+def test_cfg3_full_batch_matches_oracle():
+    """Ragged B=256 (32..4096 events per window), full size, vs the CPU oracle."""
+    from cortex.workloads import make_inputs
+
+    wl, model = _model("cfg3")
+    inp, counts = make_inputs(wl, seed=0)
+    assert counts.shape == (256,)
+    with torch.no_grad():
+        y = model(*(inp[k] for k in ("neuron_ids", "time_bins", "values", "batch_indices")))
+    p = {k: v.cpu() for k, v in model.state_dict().items()}
+    torch.set_num_threads(max(torch.get_num_threads(), 8))
+    ref = O.forward(p, wl.config, inp["neuron_ids"], inp["time_bins"], inp["values"],
+                    inp["batch_indices"])
+    assert _rel(y["behavior"], ref) <= TOL["bfloat16"]
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg3"])
+def test_windows_are_independent(name):
+    """Result of window b is bit-identical whether it runs alone or in the batch."""
+    from cortex.sharding import slice_events
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    inp, counts = make_inputs(wl, seed=1)
+    ev = {k: v.numpy() for k, v in inp.items()}
+    with torch.no_grad():
+        full = model(*(inp[k] for k in ("neuron_ids", "time_bins", "values",
+                                         "batch_indices")))["behavior"]
+        for b in (0, 5, len(counts) - 1):
+            one = slice_events(ev, counts, b, b + 1)
+            y = model(*(torch.from_numpy(one[k]) for k in ("neuron_ids", "time_bins", "values",
+                                                           "batch_indices")))["behavior"]
+            assert torch.equal(y[0], full[b]), b
+
+
+def test_interleaved_events_and_int32_indices():
+    from cortex.workloads import make_inputs
+
+    wl, model = _model("cfg1")
+    inp, counts = make_inputs(wl, seed=2, batch=8)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        base = model(*(inp[k] for k in cols))["behavior"]
+        # interleave windows while keeping each window's own event order
+        perm = torch.from_numpy(np.argsort(
+            np.concatenate([np.arange(c) * 8 + w for w, c in enumerate(counts)]), kind="stable"))
+        shuffled = model(*(inp[k][perm] for k in cols))["behavior"]
+        as32 = model(*(inp[k].int() for k in cols))["behavior"]
+    assert torch.equal(shuffled, base)
+    assert torch.equal(as32, base)
+
+
+def test_module_path_matches_fused_path():
+    """return_aux=True runs the composed module forwards (padded tokens + mask)."""
+    from cortex.workloads import make_inputs
+
+    wl, model = _model("cfg1")
+    inp, _ = make_inputs(wl, seed=3, batch=4)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        fused = model(*(inp[k] for k in cols))["behavior"]
+        mod = model(*(inp[k] for k in cols), return_aux=True)
+    assert mod["masked_spike_logits"].shape == (4, wl.config.spike_value_buckets)
+    assert _rel(mod["behavior"], fused) <= 1e-2
+
+
+def test_empty_window_inside_batch():
+    """A window with no events keeps its latents (attention over no keys is 0)."""
+    wl, model = _model("cfg1")
+    p = {k: v.cpu() for k, v in model.state_dict().items()}
+    g = torch.Generator().manual_seed(0)
+    E = 300
+    bidx = torch.cat([torch.zeros(100), torch.full((200,), 2)]).long()
+    nid = torch.randint(0, 137, (E,), generator=g)
+    tb = torch.randint(0, 600, (E,), generator=g)
+    val = torch.randint(0, 8, (E,), generator=g)
+    with torch.no_grad():
+        y = model(nid, tb, val, bidx)["behavior"]
+    ref = O.forward(p, wl.config, nid, tb, val, bidx)
+    assert y.shape == (3, 2) and torch.isfinite(y).all()
+    assert _rel(y, ref) <= TOL["bfloat16"]

@@ -1,0 +1,187 @@
+"""Host-side logic that needs no GPU: the C ABI library, argument checks, the
+workload generator, sharding, the reference-compatible module surface."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+
+def _header_functions() -> list[str]:
+    txt = open(os.path.join(ROOT, "include", "cortex_b200.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(ck_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_library_exports_every_header_symbol():
+    from cortex import _lib
+
+    lib = _lib.load()
+    names = _header_functions()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_status_strings_without_gpu():
+    from cortex import _lib
+
+    assert _lib.status_string(0) == "ok"
+    assert "index" in _lib.status_string(_lib.CK_ERR_INDEX)
+    assert "timed out" in _lib.status_string(_lib.CK_ERR_TIMEOUT)
+
+
+def test_ctypes_structs_match_header_layout(tmp_path):
+    """The ctypes mirrors must have the C layout of the header: compile a probe
+    with gcc that prints offsetof() of every field and compare."""
+    import shutil
+    import subprocess
+
+    from cortex import _lib
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    structs = {"ck_attention_args": _lib.AttentionArgs, "ck_linear_weight": _lib.LinearWeight,
+               "ck_block_weights": _lib.BlockWeights, "ck_model": _lib.Model}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "cortex_b200.h"',
+             'int main(void) {']
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    for line in out.splitlines():
+        cname, field, val = line.split()
+        py = structs[cname]
+        got = ctypes.sizeof(py) if field == "sizeof" else getattr(py, field).offset
+        assert got == int(val), (cname, field, got, val)
+
+
+def test_no_cpu_fallback():
+    from cortex.kernels.fused_rmsnorm import rms_norm_linear
+    from cortex.kernels.sparse_xattn import sparse_cross_attention
+    from cortex.kernels.tokenizer import fused_tokenizer
+
+    t = torch.randn(8, 16)
+    i = torch.zeros(4, dtype=torch.int64)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        fused_tokenizer(t, t, t, i, i, i)
+    q = torch.randn(1, 1, 4, 16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        sparse_cross_attention(q, q, q)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        rms_norm_linear(torch.randn(4, 16), torch.ones(16), torch.randn(16, 8))
+
+
+def test_model_forward_without_gpu_raises():
+    from cortex.models import CORTEX_XS, CortexModel
+
+    model = CortexModel(CORTEX_XS)
+    i = torch.zeros(4, dtype=torch.int64)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        model(i, i, i, i)
+
+
+def test_shape_validation_matches_reference():
+    from cortex.kernels.tokenizer import fused_tokenizer
+    from cortex.models import CORTEX_XS, CortexConfig, SpikeTokenizer
+
+    tok = SpikeTokenizer(CORTEX_XS)
+    with pytest.raises(ValueError, match="shape mismatch"):
+        tok(torch.zeros(10, dtype=torch.int64), torch.zeros(11, dtype=torch.int64),
+            torch.zeros(10, dtype=torch.int64))
+    t = torch.randn(8, 16)
+    with pytest.raises(ValueError, match="contiguous"):
+        fused_tokenizer(t.t().contiguous().t(), t, t, *(torch.zeros(2, dtype=torch.int64),) * 3)
+    with pytest.raises(ValueError, match="must equal hidden_dim"):
+        CortexConfig(hidden_dim=128, num_layers=2, num_heads=2, head_dim=32, num_latents=32,
+                     latent_dim=128, cross_attn_heads=2, max_neurons=256, max_time_bins=512,
+                     behavior_dim=2)
+
+
+def test_block_mask_shape_assertion():
+    from cortex.kernels.sparse_xattn import sparse_cross_attention
+
+    q = torch.randn(1, 1, 64, 16)
+    with pytest.raises(AssertionError, match="block_mask shape"):
+        sparse_cross_attention(q, q, q, torch.ones(3, 3, dtype=torch.bool), 32, 32)
+
+
+def test_workload_generator_is_deterministic_and_in_range():
+    from cortex.workloads import WORKLOADS, events_per_sample, make_events
+
+    for name, wl in WORKLOADS.items():
+        counts = events_per_sample(wl, seed=0)[:16]
+        a = make_events(counts, seed=0)
+        b = make_events(counts, seed=0)
+        for k in a:
+            assert np.array_equal(a[k], b[k]), (name, k)
+        assert a["neuron_ids"].min() >= 0 and a["neuron_ids"].max() < 137
+        assert a["time_bins"].min() >= 0 and a["time_bins"].max() < 600
+        assert a["values"].min() >= 0 and a["values"].max() <= 7
+        assert np.all(np.diff(a["batch_indices"]) >= 0)
+        off = np.concatenate([[0], np.cumsum(counts)])
+        for w in range(len(counts)):  # time bins sorted within each sample
+            assert np.all(np.diff(a["time_bins"][off[w]:off[w + 1]]) >= 0)
+    ragged = events_per_sample(WORKLOADS["cfg3"], seed=0)
+    assert ragged.shape == (256,) and ragged.min() >= 32 and ragged.max() <= 4096
+    assert 500 < ragged.mean() < 1200
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shard_bounds_cover_and_balance(world):
+    from cortex.sharding import shard_bounds
+    from cortex.workloads import WORKLOADS, events_per_sample
+
+    counts = events_per_sample(WORKLOADS["cfg3"], seed=0)
+    b = shard_bounds(counts, world)
+    assert b[0][0] == 0 and b[-1][1] == len(counts)
+    assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
+    assert all(hi > lo for lo, hi in b)
+    ev = [int(counts[lo:hi].sum()) for lo, hi in b]
+    assert max(ev) - min(ev) <= 2 * int(counts.max())
+
+
+def test_quantized_linear_storage_and_conversion():
+    from cortex.quantization.calibrate import (LayerScales, QuantizedLinear, convert_model,
+                                               count_quantized_linears, model_weight_bytes,
+                                               weight_scales)
+    from oracle import cortex_oracle as O
+
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(64, 32, bias=False)
+    torch.nn.init.normal_(lin.weight, std=0.5)
+    ql = QuantizedLinear.from_linear(lin, LayerScales(weight_scales(lin.weight), 0.01))
+    w8, sc = O.quantize_weight(lin.weight)
+    assert torch.equal(ql.weight_int8, w8) and torch.equal(ql.weight_scale, sc)
+    assert "INT8" in ql.extra_repr() and ql.weight_scale.shape == (32,)
+    model = torch.nn.Sequential(torch.nn.Linear(512, 512, bias=False))
+    fp = model_weight_bytes(model)
+    convert_model(model, {"0": LayerScales(weight_scales(model[0].weight), 1.0)})
+    assert count_quantized_linears(model) == (1, 1)
+    assert 2.5 < fp / model_weight_bytes(model) < 5.0
+
+
+def test_int8_workload_converts_exactly_the_self_attention_linears():
+    from cortex.quantization.calibrate import QuantizedLinear
+    from cortex.workloads import WORKLOADS, build_model, int8_layer_names
+
+    wl = WORKLOADS["cfg2"]
+    model = build_model(wl, "cpu")
+    q = {n for n, m in model.named_modules() if isinstance(m, QuantizedLinear)}
+    assert q == set(int8_layer_names(wl.config)) and len(q) == 28
+    assert model.tokenizer.neuron_emb.weight.dtype == torch.bfloat16
