@@ -328,6 +328,16 @@ def run_ours(args, wl):
         p99 = max_over_ranks(percentile(step_s, 99))
         p50 = max_over_ranks(percentile(step_s, 50))
         _lib.check_device_status("bench timed region")
+        if args.only_forward:  # profiling runs: just the timed forwards
+            if world > 1:
+                dist.destroy_process_group()
+            if rank == 0:
+                print(json.dumps({"metric": METRIC, "value": round(world * B * args.steps / total, 2),
+                                  "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                                  "warmup": args.warmup,
+                                  "ms_per_step": round(1e3 * total / args.steps, 4),
+                                  "mode": "forward only (profiling run)"}), flush=True)
+            return
 
         # end-to-end through the public API: pinned host inputs in, host result out
         pinned = [inp[k].pin_memory() for k in cols]
@@ -404,6 +414,8 @@ def main():
     ap.add_argument("--config", default="cfg1")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-forward", action="store_true",
+                    help="time the forwards only (no e2e / roofline / CPU legs); for ncu runs")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     from cortex.workloads import WORKLOADS

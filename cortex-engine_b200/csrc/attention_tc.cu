@@ -377,11 +377,11 @@ int attention_tc(const ck_attention_args& a, cudaStream_t st) {
 
   CUtensorMap tq, tk, tv;
   if (!make_tmap_2d(&tq, a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.q_ld, a.q_rows, a.q_ld, 64,
-                    QT, true) ||
+                    QT, 128) ||
       !make_tmap_2d(&tk, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.k_ld, a.k_rows, a.k_ld, 64,
-                    KC, true) ||
+                    KC, 128) ||
       !make_tmap_2d(&tv, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.v_ld, a.v_rows, a.v_ld, 64,
-                    KC, true))
+                    KC, 128))
     return CK_ERR_INVALID_ARG;
 
   if (!smem_attr_ready(reinterpret_cast<const void*>(attn_tc_kernel), SMEM_BYTES))

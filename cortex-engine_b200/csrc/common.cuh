@@ -81,6 +81,34 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
 }
 
+// Erf GELU for epilogues, 0.5 x (1 + erf(x / sqrt 2)), with erf evaluated by
+// Abramowitz & Stegun, Handbook of Mathematical Functions (1964), eq. 7.1.28:
+//   erf(y) = 1 - (1 + a1 y + a2 y^2 + ... + a6 y^6)^-16 + e(y),  |e| <= 3e-7, y >= 0.
+// One reciprocal and a degree-6 polynomial instead of a library erf: the GEMM
+// epilogue that applies it stays under the tensor-core time of its tile. The
+// result is rounded to bf16 right after, so the 3e-7 bound is far below the
+// output resolution; tests compare it with torch's erf GELU.
+__device__ __forceinline__ float gelu_as(float x) {
+  const float y = fminf(fabsf(x) * 0.70710678118654752440f, 1.0e4f);
+  float q = fmaf(4.30638e-5f, y, 2.765672e-4f);
+  q = fmaf(q, y, 1.520143e-4f);
+  q = fmaf(q, y, 9.2705272e-3f);
+  q = fmaf(q, y, 4.22820123e-2f);
+  q = fmaf(q, y, 7.05230784e-2f);
+  q = fmaf(q, y, 1.0f);
+  float r = __fdividef(1.0f, q);  // q >= 1
+  r = r * r;                      // r^2
+  r = r * r;                      // r^4
+  r = r * r;                      // r^8
+  r = r * r;                      // r^16 = 1 - erf(y)
+  const float h = 0.5f * x * r;  // 0.5 x (1 - erf(|x| / sqrt 2))
+  // Far in the negative tail GELU(x) = 0.5 x erfc(y) is tiny and the absolute
+  // 3e-7 bound is no longer small relative to it: use the library erfc there
+  // (x < -4 is rare after a LayerNorm, so the branch almost never diverges).
+  if (x < -4.0f) return 0.5f * x * erfcf(y);
+  return x >= 0.f ? x - h : h;
+}
+
 // ── shared-memory address helpers ────────────────────────────────────────────
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -149,6 +177,31 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
+}
+
+// Tiled TMA store shared -> global (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Wait until at most N bulk groups of this thread are still in flight.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {

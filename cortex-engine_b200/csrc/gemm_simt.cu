@@ -103,10 +103,61 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(
   }
 }
 
+// Skinny outputs (N <= 8, e.g. the behaviour head's D -> 1 projection): one warp
+// per row, lanes split K, N dot products reduced with shuffles.
+template <typename T, typename WT, int NMAX>
+__global__ void __launch_bounds__(256) gemv_rows_kernel(
+    const T* A, int64_t M, int64_t K, int64_t lda, const WT* W, int w_layout, int64_t N,
+    int64_t ldw, const float* w_scale, int epi, const T* aux, int64_t ld_aux, int64_t aux_row_mod,
+    T* Y, int64_t ldy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t m = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (m >= M) return;
+  float acc[NMAX];
+#pragma unroll
+  for (int n = 0; n < NMAX; ++n) acc[n] = 0.f;
+  for (int64_t k = lane; k < K; k += 32) {
+    const float a = tof<T>(A[m * lda + k]);
+#pragma unroll
+    for (int n = 0; n < NMAX; ++n)
+      if (n < N)
+        acc[n] = fmaf(a, tof<WT>(w_layout == CK_W_NK ? W[n * ldw + k] : W[k * ldw + n]), acc[n]);
+  }
+#pragma unroll
+  for (int n = 0; n < NMAX; ++n) acc[n] = warp_sum(acc[n]);
+  if (lane < N) {
+    float v = 0.f;
+#pragma unroll
+    for (int n = 0; n < NMAX; ++n)
+      if (n == lane) v = acc[n];
+    const int n = lane;
+    if (w_scale != nullptr) v *= w_scale[n];
+    v = rnd<T>(v);
+    if (epi == CK_EPI_GELU) {
+      v = gelu_erf(v);
+    } else if (epi == CK_EPI_RESID) {
+      const int64_t r = aux_row_mod > 0 ? m % aux_row_mod : m;
+      v = tof<T>(aux[r * ld_aux + n]) + v;
+    } else if (epi == CK_EPI_BIAS) {
+      v = v + tof<T>(aux[n]);
+    }
+    Y[m * ldy + n] = (T)v;
+  }
+}
+
 template <typename T, typename WT>
 int launch(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_layout,
            int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux, int64_t ld_aux,
            int64_t mod, void* Y, int64_t ldy, cudaStream_t st) {
+  if (N <= 8) {
+    const int64_t blocks = (M * 32 + 255) / 256;
+    if (blocks > INT32_MAX) return CK_ERR_INVALID_ARG;
+    gemv_rows_kernel<T, WT, 8><<<(unsigned)blocks, 256, 0, st>>>(
+        reinterpret_cast<const T*>(A), M, K, lda, reinterpret_cast<const WT*>(W), w_layout, N,
+        ldw, w_scale, epi, reinterpret_cast<const T*>(aux), ld_aux, mod, reinterpret_cast<T*>(Y),
+        ldy);
+    return check_launch();
+  }
   dim3 grid((unsigned)((N + TN - 1) / TN), (unsigned)((M + TM - 1) / TM));
   if (grid.y > 65535) return CK_ERR_INVALID_ARG;
   gemm_simt_kernel<T, WT><<<grid, 256, 0, st>>>(

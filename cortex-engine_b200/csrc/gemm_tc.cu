@@ -9,11 +9,13 @@
 // |w| <= 127) and the scale is applied to the fp32 accumulator.
 //
 // Structure (one persistent CTA per SM, warp-specialised):
-//   warp 0      TMA producer: A and B tiles into a STAGES-deep smem ring
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, epilogue op,
-//               bf16 store (128 threads = the 128 TMEM lanes of the tile)
-//   warps 6..9  (int8 only) int8 -> bf16 converter
+//   warp 0       TMA producer: A and B tiles into a STAGES-deep smem ring
+//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..9   epilogue: two warps per TMEM lane quarter, each taking half of
+//                the tile's columns: tcgen05.ld of the fp32 accumulator, the
+//                epilogue op (scale, bf16 rounding, GELU / residual / bias),
+//                staging in 64B-swizzled smem and a TMA tile store
+//   warps 10..13 (int8 only) int8 -> bf16 converter
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1. All mbarrier waits are bounded
 // (common.cuh); a timeout raises a CTA-wide abort flag and every role drains.
@@ -29,6 +31,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int EPI_WARPS = 8;
+constexpr int STG_BYTES = 32 * 32 * 2;  // one 32x32 bf16 staging tile
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
@@ -38,49 +42,56 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
   static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
-  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
-  static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
-  static constexpr int NUM_THREADS = (WMODE == W_I8_NK) ? 320 : 192;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr int EPI_SMEM = EPI_WARPS * 2 * STG_BYTES;  // double-buffered per warp
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
+  static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
+  static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
+  static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
 };
 
 struct GemmArgs {
   int M, N, K;
   int num_m_tiles, num_n_tiles, num_k_blocks;
-  __nv_bfloat16* Y;
-  int64_t ldy;
   const __nv_bfloat16* aux;
   int64_t ld_aux;
   int64_t aux_row_mod;
   const float* w_scale;
+  int scale_vec;  // w_scale is 16-byte aligned: vector loads
 };
 
-__device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int m, int n0, const float* v,
-                                                int epi) {
-  // v: 32 fp32 accumulators for columns n0 .. n0+31 of row m.
-  float out[32];
+// Epilogue math for 32 consecutive columns n0.. of row m (v: fp32 accumulators).
+template <int EPI>
+__device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, float* v) {
   const bool full = (n0 + 32 <= p.N);
-  float scale[32];
   if (p.w_scale != nullptr) {
+    if (full && p.scale_vec) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) scale[i] = (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
+      for (int c = 0; c < 8; ++c) {
+        const float4 s = __ldg(reinterpret_cast<const float4*>(p.w_scale + n0) + c);
+        v[4 * c] *= s.x;
+        v[4 * c + 1] *= s.y;
+        v[4 * c + 2] *= s.z;
+        v[4 * c + 3] *= s.w;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i) v[i] *= (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
+    }
   }
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float a = v[i];
-    if (p.w_scale != nullptr) a *= scale[i];
-    out[i] = rbf(a);  // linear output in bf16, as F.linear returns it
-  }
-  if (epi == CK_EPI_GELU) {
+  for (int i = 0; i < 32; ++i) v[i] = rbf(v[i]);  // linear output in bf16, as F.linear returns it
+  if (EPI == CK_EPI_GELU) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) out[i] = gelu_erf(out[i]);
-  } else if (epi == CK_EPI_RESID || epi == CK_EPI_BIAS) {
+    for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
+  } else if (EPI == CK_EPI_RESID || EPI == CK_EPI_BIAS) {
+    if (m >= p.M) return;
     const __nv_bfloat16* src;
-    if (epi == CK_EPI_RESID) {
-      int64_t r = p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;
+    if (EPI == CK_EPI_RESID) {
+      const int64_t r = p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;
       src = p.aux + r * p.ld_aux + n0;
     } else {
       src = p.aux + n0;
@@ -88,32 +99,22 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int m, int n0
     if (full) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint4 raw = *reinterpret_cast<const uint4*>(src + 8 * c);
         float f[8];
-        unpack8(raw, f);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(src) + c), f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) out[8 * c + j] = f[j] + out[8 * c + j];
+        for (int j = 0; j < 8; ++j) v[8 * c + j] = f[j] + v[8 * c + j];
       }
     } else {
       for (int i = 0; i < 32; ++i)
-        if (n0 + i < p.N) out[i] = bf2f(src[i]) + out[i];
+        if (n0 + i < p.N) v[i] = bf2f(src[i]) + v[i];
     }
-  }
-  __nv_bfloat16* dst = p.Y + (int64_t)m * p.ldy + n0;
-  if (full) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<uint4*>(dst + 8 * c) = pack8(out + 8 * c);
-  } else {
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < p.N) dst[i] = f2bf(out[i]);
   }
 }
 
 template <int BN, int WMODE, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs p) {
+                   const __grid_constant__ CUtensorMap tmY, const GemmArgs p) {
   using C = GemmCfg<BN, WMODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -121,7 +122,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::STAGES * C::A_BYTES;
   uint8_t* sB8 = sB + C::STAGES * C::B_BYTES;
-  uint8_t* sBar = sB8 + C::STAGES * C::B8_BYTES;
+  uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
+  uint8_t* sBar = sStg + C::EPI_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
   uint64_t* conv = empty + C::STAGES;
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmY);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -195,9 +198,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
       }
       // Drain: make sure every issued copy has landed before the CTA can exit.
       for (int s = 0; s < C::STAGES && s < issued; ++s) {
-        int last = issued - 1 - ((issued - 1 - s) % C::STAGES);  // last load index into stage s
-        uint32_t par = (uint32_t)((last / C::STAGES) & 1);
-        mbar_wait(&full[s], par, nullptr, 9);
+        const int last = issued - 1 - ((issued - 1 - s) % C::STAGES);
+        mbar_wait(&full[s], (uint32_t)((last / C::STAGES) & 1), nullptr, 9);
       }
     }
   } else if (warp == 1) {
@@ -223,10 +225,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            uint64_t adesc = sw128_desc(a_addr + k * 32, 16, 1024);
-            uint64_t bdesc = (WMODE == W_BF16_KN)
-                                 ? sw128_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
-                                 : sw128_desc(b_addr + k * 32, 16, 1024);
+            const uint64_t adesc = sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = (WMODE == W_BF16_KN)
+                                       ? sw128_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
+                                       : sw128_desc(b_addr + k * 32, 16, 1024);
             tc_mma_ss(d_tmem, adesc, bdesc, C::IDESC, (kb | k) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
@@ -244,10 +246,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
       tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 8);
     }
-  } else if (warp >= 2 && warp < 6) {
-    // ── epilogue ──
+  } else if (warp < C::CONV_WARP0) {
+    // ── epilogue: 8 warps, (lane quarter, column half) each ──
+    const int e = warp - 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = e >> 2;
     const int row = quarter * 32 + lane;
+    uint8_t* stg = sStg + e * 2 * STG_BYTES;
+    int sbuf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -256,23 +262,41 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
       tc_fence_after();
       const int m = mt * BM + row;
+      const int m0 = mt * BM + quarter * 32;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n0 = nt * BN + c * 32;
+      for (int c = 0; c < BN / 64; ++c) {
+        const int col = half * (BN / 2) + c * 32;
+        const int n0 = nt * BN + col;
         float v[32];
-        tmem_ld32(tbase + (uint32_t)(c * 32), v);
+        tmem_ld32(tbase + (uint32_t)col, v);
         tc_wait_ld();
-        if (m < p.M && n0 < p.N) store_row_chunk(p, m, n0, v, EPI);
+        if (n0 < p.N) epilogue_math<EPI>(p, m, n0, v);
+        // stage the 32x32 tile (64-byte rows, 64B swizzle) and store it with TMA
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        uint8_t* buf = stg + sbuf * STG_BYTES;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+              pack8(v + 8 * q);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && n0 < p.N && m0 < p.M) {
+          tma_store_2d(&tmY, buf, n0, m0);
+          bulk_commit();
+        }
+        sbuf ^= 1;
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) bulk_wait<0>();  // stores complete before the CTA exits
   } else if (WMODE == W_I8_NK) {
-    // ── int8 -> bf16 converter (warps 6..9) ──
-    const int t = threadIdx.x - 192;
+    // ── int8 -> bf16 converter (4 warps) ──
+    const int t = threadIdx.x - 32 * C::CONV_WARP0;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -313,62 +337,28 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
   }
 }
 
-// ── host side ────────────────────────────────────────────────────────────────
-
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-}  // namespace
-
-bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
-                  uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t box_inner,
-                  uint32_t box_outer, bool swizzle128) {
-  auto fn = get_encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld_elems * (uint64_t)elem_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-namespace {
-
 template <int BN, int WMODE, int EPI>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
-                cudaStream_t st) {
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
+                const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<BN, WMODE>;
+  static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
   auto kern = gemm_tc_kernel<BN, WMODE, EPI>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
     return record_cuda_error();
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, a);
+  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, ty, a);
   return check_launch();
 }
 
 template <int BN, int WMODE>
-int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
-                 cudaStream_t st) {
+int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
+                 const GemmArgs& a, cudaStream_t st) {
   switch (epi) {
-    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE>(ta, tb, a, st);
-    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU>(ta, tb, a, st);
-    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID>(ta, tb, a, st);
-    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS>(ta, tb, a, st);
+    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE>(ta, tb, ty, a, st);
+    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU>(ta, tb, ty, a, st);
+    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID>(ta, tb, ty, a, st);
+    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS>(ta, tb, ty, a, st);
   }
   return CK_ERR_INVALID_ARG;
 }
@@ -408,35 +398,36 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.num_m_tiles = (int)((M + BM - 1) / BM);
   a.num_n_tiles = (int)((N + BN - 1) / BN);
   a.num_k_blocks = (int)((K + BK - 1) / BK);
-  a.Y = reinterpret_cast<__nv_bfloat16*>(Y);
-  a.ldy = ldy;
   a.aux = reinterpret_cast<const __nv_bfloat16*>(aux);
   a.ld_aux = ld_aux;
   a.aux_row_mod = aux_row_mod;
   a.w_scale = (w_dtype == CK_I8) ? w_scale : nullptr;
   if (w_dtype == CK_I8 && w_scale == nullptr) return CK_ERR_INVALID_ARG;
+  a.scale_vec = (reinterpret_cast<uintptr_t>(w_scale) & 15u) == 0;
 
-  CUtensorMap ta, tb;
-  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, true))
+  CUtensorMap ta, tb, ty;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
+    return CK_ERR_INVALID_ARG;
+  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 32, 32, 64))
     return CK_ERR_INVALID_ARG;
   bool ok;
   if (w_dtype == CK_I8) {
-    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldw, BK, BN, false);
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldw, BK, BN, 0);
   } else if (w_layout == CK_W_NK) {
-    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, ldw, BK, BN, true);
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, ldw, BK, BN, 128);
   } else {
-    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, 64, BK, true);
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, 64, BK, 128);
   }
   if (!ok) return CK_ERR_INVALID_ARG;
 
   if (BN == 256) {
-    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, ta, tb, a, st);
-    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, ta, tb, a, st);
-    return dispatch_epi<256, W_BF16_KN>(epi, ta, tb, a, st);
+    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, ta, tb, ty, a, st);
+    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, ta, tb, ty, a, st);
+    return dispatch_epi<256, W_BF16_KN>(epi, ta, tb, ty, a, st);
   }
-  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, ta, tb, a, st);
-  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, ta, tb, a, st);
-  return dispatch_epi<128, W_BF16_KN>(epi, ta, tb, a, st);
+  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, ta, tb, ty, a, st);
+  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, ta, tb, ty, a, st);
+  return dispatch_epi<128, W_BF16_KN>(epi, ta, tb, ty, a, st);
 }
 
 }  // namespace ck

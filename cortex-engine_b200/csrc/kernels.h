@@ -17,7 +17,7 @@ bool smem_attr_ready(const void* kernel, int bytes);  // per device, once
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                   uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t box_inner,
-                  uint32_t box_outer, bool swizzle128);
+                  uint32_t box_outer, int swizzle_bytes /* 0, 64 or 128 */);
 
 // tcgen05 GEMM (gemm_tc.cu)
 bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_layout, int64_t N,

@@ -232,6 +232,39 @@ def test_linear_tc_int8(M, K, N):
     _status_ok()
 
 
+@pytest.mark.parametrize("M,K,N", [(64, 512, 1), (1000, 768, 3), (7, 33, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_linear_skinny(M, K, N, dtype):
+    from cortex.kernels import _ops
+
+    torch.manual_seed(N)
+    x = torch.randn(M, K, dtype=dtype)
+    w = (torch.randn(N, K) / math.sqrt(K)).to(dtype)
+    out = _ops.linear(x.to(DEV), w.to(DEV)).cpu()
+    ref = (x.float() @ w.float().t()).to(dtype)
+    tol = (1e-5, 1e-5) if dtype == torch.float32 else (1e-2, 1e-2)
+    torch.testing.assert_close(out, ref, rtol=tol[0], atol=tol[1])
+
+
+def test_gelu_epilogue_matches_torch_erf_gelu():
+    """The A&S 7.1.28 GELU in the GEMM epilogue vs torch's exact-erf GELU on the
+    same bf16 pre-activations: identical except rare last-bit rounding flips."""
+    from cortex import _lib as L
+    from cortex.kernels import _ops
+
+    torch.manual_seed(5)
+    M, K, N = 2048, 512, 2048
+    x = torch.randn(M, K, dtype=torch.bfloat16) * 2
+    w = (torch.randn(N, K) / math.sqrt(K)).to(torch.bfloat16)
+    pre = _ops.linear(x.to(DEV), w.to(DEV)).float()
+    out = _ops.linear(x.to(DEV), w.to(DEV), epi=L.CK_EPI_GELU).float()
+    ref = torch.nn.functional.gelu(pre).to(torch.bfloat16).float()
+    diff = (out - ref).abs()
+    ulp = ref.abs().clamp_min(1e-30) * 2 ** -7
+    assert bool((diff <= ulp + 1e-30).all()), float((diff / ulp).max())
+    assert (diff > 0).float().mean().item() < 1e-3
+
+
 @pytest.mark.parametrize("epi", ["gelu", "resid", "resid_mod", "bias"])
 def test_linear_epilogues(epi):
     from cortex import _lib as L
