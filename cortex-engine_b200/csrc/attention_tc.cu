@@ -1,15 +1,19 @@
 // tcgen05 attention for head_dim 64, bf16 (B200, sm_100a).
 //
-// One CTA (128 threads) per (batch b, head h, 128-query tile). The query tile
-// is loaded once by TMA; keys and values stream in 128-key chunks through a
-// double-buffered TMA ring. Per chunk:
-//   S  = Q K^T        tcgen05.mma M=128 N=128 K=64   -> TMEM cols [0,128)
-//   softmax           each thread owns one query row (its TMEM lane): scores
-//                     are masked (key count, optional tile mask), the running
-//                     max/sum updated in fp32 and P = exp2(s - m) written to
-//                     smem as bf16 in the 128B-swizzled K-major layout
-//   O_j = P V         tcgen05.mma M=128 N=64 K=128  -> TMEM cols [128,192)
-//   o  = o*alpha + O_j   in registers (fp32)
+// One CTA (128 threads, two CTAs per SM) per (batch b, head h, 128-query tile).
+// The query tile is loaded once by TMA; keys and values stream in 128-key chunks
+// through two K and two V buffers with separate barriers, so a K buffer is
+// refilled as soon as its S = Q K^T product is done and a V buffer as soon as
+// its P V product is done. Per chunk k:
+//   S_k = Q K_k^T     tcgen05.mma M=128 N=128 K=64   -> TMEM cols [0,128)
+//   softmax           thread r owns query row r (its TMEM lane): the 128 scores
+//                     are loaded with four tcgen05.ld and one wait, masked,
+//                     reduced with short independent chains (max, sum),
+//                     exponentiated with ex2, rounded to bf16 and written as P
+//                     into smem (128B-swizzled K-major operand layout)
+//   O_k = P_k V_k     tcgen05.mma M=128 N=64 K=128  -> TMEM cols [128,192)
+//   o = o * alpha + O  in registers, one chunk late: O_{k-1} is read back after
+//                     the softmax of chunk k, so the P V product overlaps it.
 // Chunks with no unmasked (query, key) pair for this tile are never loaded.
 // Keys of a packed varlen batch start at key_offsets[b]; rows past the last
 // event are masked, and the tensor map ends at the last real row so that TMA
@@ -17,7 +21,8 @@
 //
 // This covers the Perceiver cross-attention (latent queries over packed spike
 // keys, cortex/models/perceiver.py:54-82), the latent self-attention
-// (cortex/models/perceiver.py:107-126) and the block-sparse kernel API
+// (cortex/models/perceiver.py:107-126), the behaviour head's query attention
+// (cortex/models/cortex.py:44-49) and the block-sparse kernel API
 // (cortex/kernels/sparse_xattn.py:205-334).
 #include <cuda.h>
 
@@ -31,10 +36,10 @@ namespace {
 constexpr int QT = 128;  // queries per CTA
 constexpr int KC = 128;  // keys per chunk
 constexpr int DH = 64;
-constexpr int TILE_BYTES = QT * DH * 2;  // 16 KB (also K/V chunk size)
+constexpr int TILE_BYTES = QT * DH * 2;  // 16 KB (also one K or V chunk)
 constexpr int P_BYTES = QT * KC * 2;     // 32 KB
-// Two CTAs per SM: 2 x (114816 + 1024 reserved) <= 228 KB. The dynamic smem base
-// is 1024-byte aligned (no static smem in this kernel); the kernel checks it.
+// Two CTAs per SM: 2 x (SMEM_BYTES + 1 KB reserved) <= 228 KB. The dynamic smem
+// base is 1024-byte aligned (no static smem in this kernel); the kernel checks it.
 constexpr int SMEM_BYTES = TILE_BYTES * 5 + P_BYTES + 128;
 constexpr uint32_t IDESC_S = idesc_bf16(128, 128, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(128, 64, 1);
@@ -54,6 +59,13 @@ struct TcAttnArgs {
   float scale_log2;
 };
 
+// 2^x with the hardware approximation (ex2.approx(-inf) = +0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ bool chunk_active(const TcAttnArgs& p, int l0, int l1, int j, int nk) {
   const int e0 = j * KC;
   if (e0 >= nk) return false;
@@ -72,6 +84,32 @@ __device__ __forceinline__ int next_active(const TcAttnArgs& p, int l0, int l1, 
   return -1;
 }
 
+// 128 validity bits of this thread's query row for keys e0 .. e0+127.
+__device__ __forceinline__ void key_bits(const TcAttnArgs& p, const uint8_t* mask_row,
+                                         const uint8_t* kmask, int e0, int nk, uint32_t* vb) {
+  const int lim = nk - e0;  // keys past the sample are invalid
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const int lo = w * 32;
+    vb[w] = (lim <= lo) ? 0u : (lim >= lo + 32 ? 0xffffffffu : ((1u << (lim - lo)) - 1u));
+  }
+  if (mask_row != nullptr) {
+    const int t0 = e0 / p.block_e;
+    const int t1 = (min(e0 + KC, nk) - 1) / p.block_e;
+    for (int t = t0; t <= t1; ++t) {
+      if (mask_row[t]) continue;
+      const int a = max(t * p.block_e - e0, 0);
+      const int b = min((t + 1) * p.block_e - e0, KC);
+      for (int c = a; c < b; ++c) vb[c >> 5] &= ~(1u << (c & 31));
+    }
+  }
+  if (kmask != nullptr) {
+    for (int c = 0; c < KC && c < lim; ++c)
+      if (!kmask[e0 + c]) vb[c >> 5] &= ~(1u << (c & 31));
+  }
+}
+
+template <bool MASKED>
 __global__ void __launch_bounds__(128, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const TcAttnArgs p) {
@@ -80,18 +118,18 @@ __global__ void __launch_bounds__(128, 2)
     if (threadIdx.x == 0) set_status(CK_ERR_INVALID_ARG, 1024, (int)(smem_u32(smem_raw) & 1023u));
     return;
   }
-  uint8_t* smem = smem_raw;
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TILE_BYTES;            // 2 buffers
-  uint8_t* sV = sK + 2 * TILE_BYTES;        // 2 buffers
-  uint8_t* sP = sV + 2 * TILE_BYTES;        // 2 x 16 KB atoms (keys 0..63, 64..127)
+  uint8_t* sQ = smem_raw;
+  uint8_t* sK = sQ + TILE_BYTES;      // 2 buffers
+  uint8_t* sV = sK + 2 * TILE_BYTES;  // 2 buffers
+  uint8_t* sP = sV + 2 * TILE_BYTES;  // 2 x 16 KB atoms (keys 0..63, 64..127)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;  // [2]
-  uint64_t* s_full = bars + 3;
-  uint64_t* o_full = bars + 4;
-  uint64_t* drain = bars + 5;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  uint64_t* k_full = bars + 1;  // [2]
+  uint64_t* v_full = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* o_full = bars + 6;
+  uint64_t* drain = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -125,8 +163,10 @@ __global__ void __launch_bounds__(128, 2)
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+    }
     mbar_init(s_full, 1);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
@@ -148,33 +188,43 @@ __global__ void __launch_bounds__(128, 2)
   const int row = warp * 32 + lane;  // query row within the tile == TMEM lane
   const int l = l0 + row;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint8_t* mask_row = nullptr;
+  const uint8_t* kmask = nullptr;
+  if (MASKED) {
+    if (p.block_mask != nullptr && l < p.Lq)
+      mask_row = p.block_mask + (int64_t)(l / p.block_l) * p.n_k_tiles;
+    if (p.key_mask != nullptr) kmask = p.key_mask + (int64_t)b * p.key_mask_ld;
+  }
 
   float o_acc[DH];
 #pragma unroll
   for (int i = 0; i < DH; ++i) o_acc[i] = 0.f;
   float m_i = -INFINITY;
   float l_i = 0.f;
-  int tma_issued[2] = {0, 0};  // loads issued per K/V buffer (thread 0 only)
-  bool q_issued = false;
+  float alpha_pend = 0.f;  // rescale factor that goes with the O not yet added
+  int k_loads0 = 0, k_loads1 = 0, v_loads0 = 0, v_loads1 = 0;  // thread 0 only
 
-  int j = next_active(p, l0, l1, 0, nk);
-  if (tid == 0 && j >= 0) {
+  // chunk schedule: current, next and the one after (active chunks only)
+  int c_cur = next_active(p, l0, l1, 0, nk);
+  int c_next = c_cur >= 0 ? next_active(p, l0, l1, c_cur + 1, nk) : -1;
+  int c_next2 = c_next >= 0 ? next_active(p, l0, l1, c_next + 1, nk) : -1;
+
+  if (tid == 0 && c_cur >= 0) {
     mbar_arrive_expect_tx(q_full, TILE_BYTES);
     tma_load_2d(sQ, &tmQ, q_full, q_col, q_row);
-    q_issued = true;
-    mbar_arrive_expect_tx(&kv_full[0], 2 * TILE_BYTES);
-    tma_load_2d(sK, &tmK, &kv_full[0], k_col, k_row_h + j * KC);
-    tma_load_2d(sV, &tmV, &kv_full[0], v_col, v_row_h + j * KC);
-    tma_issued[0] = 1;
-    int j1 = next_active(p, l0, l1, j + 1, nk);
-    if (j1 >= 0) {
-      mbar_arrive_expect_tx(&kv_full[1], 2 * TILE_BYTES);
-      tma_load_2d(sK + TILE_BYTES, &tmK, &kv_full[1], k_col, k_row_h + j1 * KC);
-      tma_load_2d(sV + TILE_BYTES, &tmV, &kv_full[1], v_col, v_row_h + j1 * KC);
-      tma_issued[1] = 1;
+    mbar_arrive_expect_tx(&k_full[0], TILE_BYTES);
+    tma_load_2d(sK, &tmK, &k_full[0], k_col, k_row_h + c_cur * KC);
+    mbar_arrive_expect_tx(&v_full[0], TILE_BYTES);
+    tma_load_2d(sV, &tmV, &v_full[0], v_col, v_row_h + c_cur * KC);
+    k_loads0 = v_loads0 = 1;
+    if (c_next >= 0) {
+      mbar_arrive_expect_tx(&k_full[1], TILE_BYTES);
+      tma_load_2d(sK + TILE_BYTES, &tmK, &k_full[1], k_col, k_row_h + c_next * KC);
+      mbar_arrive_expect_tx(&v_full[1], TILE_BYTES);
+      tma_load_2d(sV + TILE_BYTES, &tmV, &v_full[1], v_col, v_row_h + c_next * KC);
+      k_loads1 = v_loads1 = 1;
     }
-    bool ok = mbar_wait(q_full, 0, abort_flag, 20) && mbar_wait(&kv_full[0], 0, abort_flag, 21);
-    if (ok) {
+    if (mbar_wait(q_full, 0, abort_flag, 20) && mbar_wait(&k_full[0], 0, abort_flag, 21)) {
       tc_fence_after();
       const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK);
 #pragma unroll
@@ -185,117 +235,137 @@ __global__ void __launch_bounds__(128, 2)
     }
   }
 
-  const uint8_t* mask_row = nullptr;
-  if (p.block_mask != nullptr && l < p.Lq)
-    mask_row = p.block_mask + (int64_t)(l / p.block_l) * p.n_k_tiles;
-  const uint8_t* kmask = (p.key_mask != nullptr) ? p.key_mask + (int64_t)b * p.key_mask_ld : nullptr;
-
   int it = 0;
-  while (j >= 0) {
+  bool ok = true;
+  while (c_cur >= 0) {
     const int buf = it & 1;
-    if (!mbar_wait(s_full, (uint32_t)(it & 1), abort_flag, 22)) break;
-    tc_fence_after();
-    const int e0 = j * KC;
-    // pass 1: masked row max of this chunk
-    float cmax = -INFINITY;
-#pragma unroll 1
-    for (int g = 0; g < 4; ++g) {
-      float s[32];
-      tmem_ld32(tmem_s + lane_off + g * 32, s);
-      tc_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int e = e0 + g * 32 + c;
-        bool valid = e < nk;
-        if (mask_row != nullptr && valid) valid = mask_row[e / p.block_e] != 0;
-        if (kmask != nullptr && valid) valid = kmask[e] != 0;
-        if (valid) cmax = fmaxf(cmax, s[c] * p.scale_log2);
-      }
+    if (!mbar_wait(s_full, (uint32_t)(it & 1), abort_flag, 22)) {
+      ok = false;
+      break;
     }
+    tc_fence_after();
+    // K buffer `buf` is free once S_it is done: prefetch the chunk two ahead
+    if (tid == 0 && c_next2 >= 0) {
+      mbar_arrive_expect_tx(&k_full[buf], TILE_BYTES);
+      tma_load_2d(sK + buf * TILE_BYTES, &tmK, &k_full[buf], k_col, k_row_h + c_next2 * KC);
+      if (buf) ++k_loads1; else ++k_loads0;
+    }
+    float s[KC];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) tmem_ld32(tmem_s + lane_off + g * 32, s + 32 * g);
+    tc_wait_ld();
+    const int e0 = c_cur * KC;
+    if (MASKED) {
+      uint32_t vb[4];
+      key_bits(p, mask_row, kmask, e0, nk, vb);
+#pragma unroll
+      for (int c = 0; c < KC; ++c)
+        if (!((vb[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
+    } else if (e0 + KC > nk) {
+      const int lim = nk - e0;
+#pragma unroll
+      for (int c = 0; c < KC; ++c)
+        if (c >= lim) s[c] = -INFINITY;
+    }
+    // row max over 8 independent chains, new running max, rescale factor
+    float t[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) t[c] = s[c];
+#pragma unroll
+    for (int c = 8; c < KC; ++c) t[c & 7] = fmaxf(t[c & 7], s[c]);
+    const float cmax = fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])),
+                             fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7]))) *
+                       p.scale_log2;  // scale > 0: max commutes with it
     const float m_new = fmaxf(m_i, cmax);
     const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-    const float alpha = (m_i == -INFINITY) ? 0.f : exp2f(m_i - m_use);
-    // pass 2: probabilities -> bf16 P tile, row sum
-    float psum = 0.f;
-#pragma unroll 1
-    for (int g = 0; g < 4; ++g) {
-      float s[32];
-      tmem_ld32(tmem_s + lane_off + g * 32, s);
-      tc_wait_ld();
-      float pr[32];
+    const float alpha = (m_i == -INFINITY) ? 0.f : ex2(m_i - m_use);
+    // probabilities and their sum
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int e = e0 + g * 32 + c;
-        bool valid = e < nk;
-        if (mask_row != nullptr && valid) valid = mask_row[e / p.block_e] != 0;
-        if (kmask != nullptr && valid) valid = kmask[e] != 0;
-        pr[c] = valid ? exp2f(s[c] * p.scale_log2 - m_use) : 0.f;
-        psum += pr[c];
-      }
-      uint8_t* atom = sP + (g >> 1) * (QT * 128);
+    for (int c = 0; c < KC; ++c) s[c] = ex2(fmaf(s[c], p.scale_log2, -m_use));
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4)
-        *reinterpret_cast<uint4*>(atom + sw128_off(row, (g & 1) * 4 + q4)) = pack8(pr + 8 * q4);
-    }
-    l_i = l_i * alpha + psum;
+    for (int c = 0; c < 8; ++c) t[c] = s[c];
+#pragma unroll
+    for (int c = 8; c < KC; ++c) t[c & 7] += s[c];
+    l_i = l_i * alpha + (((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7])));
     m_i = m_new;
+
+    // P_{it-1} and V of chunk it-1 are released once the previous P V is done
+    if (it > 0 && !mbar_wait(o_full, (uint32_t)((it - 1) & 1), abort_flag, 24)) {
+      ok = false;
+      break;
+    }
+    // P_it -> smem (bf16, 128B swizzle, keys 0..63 in atom 0, 64..127 in atom 1)
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      uint8_t* atom = sP + (g >> 3) * (QT * 128);
+      *reinterpret_cast<uint4*>(atom + sw128_off(row, g & 7)) = pack8(s + 8 * g);
+    }
     fence_proxy_async_smem();
+    if (it > 0) {
+      // add the previous chunk's O (TMEM is rewritten only after the barrier below)
+      tc_fence_after();
+      float ov[DH];
+      tmem_ld32(tmem_o + lane_off, ov);
+      tmem_ld32(tmem_o + lane_off + 32, ov + 32);
+      tc_wait_ld();
+#pragma unroll
+      for (int i = 0; i < DH; ++i) o_acc[i] = fmaf(o_acc[i], alpha_pend, ov[i]);
+      // V buffer of chunk it-1 is free: load the next chunk's V into it
+      if (tid == 0 && c_next >= 0) {
+        const int vb_ = buf ^ 1;
+        mbar_arrive_expect_tx(&v_full[vb_], TILE_BYTES);
+        tma_load_2d(sV + vb_ * TILE_BYTES, &tmV, &v_full[vb_], v_col, v_row_h + c_next * KC);
+        if (vb_) ++v_loads1; else ++v_loads0;
+      }
+    }
+    alpha_pend = alpha;
     tc_fence_before();
     __syncthreads();
 
-    int jn = -1;
     if (tid == 0) {
       tc_fence_after();
-      // O_j = P V_j
-      const uint32_t pa = smem_u32(sP), va = smem_u32(sV + buf * TILE_BYTES);
+      // O_it = P_it V_it
+      if (mbar_wait(&v_full[buf], (uint32_t)((it >> 1) & 1), abort_flag, 25)) {
+        const uint32_t pa = smem_u32(sP), va = smem_u32(sV + buf * TILE_BYTES);
 #pragma unroll
-      for (int k = 0; k < KC / 16; ++k) {
-        uint64_t adesc = sw128_desc(pa + (k >> 2) * (QT * 128) + (k & 3) * 32, 16, 1024);
-        uint64_t bdesc = sw128_desc(va + k * 16 * 128, 8192, 1024);
-        tc_mma_ss(tmem_o, adesc, bdesc, IDESC_O, k != 0);
-      }
-      tc_commit(o_full);
-      // S_{next} = Q K_next (next chunk already in the other buffer)
-      jn = next_active(p, l0, l1, j + 1, nk);
-      if (jn >= 0) {
-        const int nb = buf ^ 1;
-        if (mbar_wait(&kv_full[nb], (uint32_t)(((it + 1) >> 1) & 1), abort_flag, 23)) {
-          tc_fence_after();
-          const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + nb * TILE_BYTES);
-#pragma unroll
-          for (int k = 0; k < DH / 16; ++k)
-            tc_mma_ss(tmem_s, sw128_desc(qa + k * 32, 16, 1024),
-                      sw128_desc(ka + k * 32, 16, 1024), IDESC_S, k != 0);
-          tc_commit(s_full);
+        for (int k = 0; k < KC / 16; ++k) {
+          const uint64_t adesc = sw128_desc(pa + (k >> 2) * (QT * 128) + (k & 3) * 32, 16, 1024);
+          const uint64_t bdesc = sw128_desc(va + k * 16 * 128, 8192, 1024);
+          tc_mma_ss(tmem_o, adesc, bdesc, IDESC_O, k != 0);
         }
+        tc_commit(o_full);
+      }
+      // S_{it+1} = Q K_{it+1}^T
+      if (c_next >= 0 &&
+          mbar_wait(&k_full[buf ^ 1], (uint32_t)(((it + 1) >> 1) & 1), abort_flag, 23)) {
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + (buf ^ 1) * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < DH / 16; ++k)
+          tc_mma_ss(tmem_s, sw128_desc(qa + k * 32, 16, 1024), sw128_desc(ka + k * 32, 16, 1024),
+                    IDESC_S, k != 0);
+        tc_commit(s_full);
       }
     }
-    if (!mbar_wait(o_full, (uint32_t)(it & 1), abort_flag, 24)) break;
-    tc_fence_after();
-#pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      float ov[32];
-      tmem_ld32(tmem_o + lane_off + g * 32, ov);
-      tc_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 32; ++c) o_acc[g * 32 + c] = o_acc[g * 32 + c] * alpha + ov[c];
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && jn >= 0) {
-      // prefetch the chunk after next into the buffer PV_j has finished with
-      const int j2 = next_active(p, l0, l1, jn + 1, nk);
-      if (j2 >= 0) {
-        mbar_arrive_expect_tx(&kv_full[buf], 2 * TILE_BYTES);
-        tma_load_2d(sK + buf * TILE_BYTES, &tmK, &kv_full[buf], k_col, k_row_h + j2 * KC);
-        tma_load_2d(sV + buf * TILE_BYTES, &tmV, &kv_full[buf], v_col, v_row_h + j2 * KC);
-        tma_issued[buf] += 1;
-      }
-    }
-    // all threads agree on the next chunk (same deterministic scan)
-    j = next_active(p, l0, l1, j + 1, nk);
+    c_cur = c_next;
+    c_next = c_next2;
+    c_next2 = c_next2 >= 0 ? next_active(p, l0, l1, c_next2 + 1, nk) : -1;
     ++it;
-    if (*abort_flag) break;
+    if (*abort_flag) {
+      ok = false;
+      break;
+    }
+  }
+
+  // the last chunk's O
+  if (ok && it > 0 && mbar_wait(o_full, (uint32_t)((it - 1) & 1), abort_flag, 26)) {
+    tc_fence_after();
+    float ov[DH];
+    tmem_ld32(tmem_o + lane_off, ov);
+    tmem_ld32(tmem_o + lane_off + 32, ov + 32);
+    tc_wait_ld();
+#pragma unroll
+    for (int i = 0; i < DH; ++i) o_acc[i] = fmaf(o_acc[i], alpha_pend, ov[i]);
   }
 
   // store the normalised output row
@@ -317,9 +387,11 @@ __global__ void __launch_bounds__(128, 2)
   if (tid == 0) {
     tc_commit(drain);
     mbar_wait(drain, 0, nullptr, 28);
-    if (q_issued) mbar_wait(q_full, 0, nullptr, 29);
-    for (int bb = 0; bb < 2; ++bb)
-      if (tma_issued[bb] > 0) mbar_wait(&kv_full[bb], (uint32_t)((tma_issued[bb] - 1) & 1), nullptr, 30);
+    if (k_loads0 > 0) mbar_wait(q_full, 0, nullptr, 29);
+    if (k_loads0 > 0) mbar_wait(&k_full[0], (uint32_t)((k_loads0 - 1) & 1), nullptr, 30);
+    if (k_loads1 > 0) mbar_wait(&k_full[1], (uint32_t)((k_loads1 - 1) & 1), nullptr, 30);
+    if (v_loads0 > 0) mbar_wait(&v_full[0], (uint32_t)((v_loads0 - 1) & 1), nullptr, 31);
+    if (v_loads1 > 0) mbar_wait(&v_full[1], (uint32_t)((v_loads1 - 1) & 1), nullptr, 31);
   }
   tc_fence_before();
   __syncthreads();
@@ -384,12 +456,17 @@ int attention_tc(const ck_attention_args& a, cudaStream_t st) {
                     KC, 128))
     return CK_ERR_INVALID_ARG;
 
-  if (!smem_attr_ready(reinterpret_cast<const void*>(attn_tc_kernel), SMEM_BYTES))
-    return record_cuda_error();
+  const bool masked = a.block_mask != nullptr || a.key_mask != nullptr;
+  const void* kern = masked ? reinterpret_cast<const void*>(attn_tc_kernel<true>)
+                            : reinterpret_cast<const void*>(attn_tc_kernel<false>);
+  if (!smem_attr_ready(kern, SMEM_BYTES)) return record_cuda_error();
   const int64_t blocks = (int64_t)p.num_q_tiles * a.H * a.B;
   if (blocks <= 0) return CK_OK;
   if (blocks > INT32_MAX) return CK_ERR_INVALID_ARG;
-  attn_tc_kernel<<<(unsigned)blocks, 128, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  if (masked)
+    attn_tc_kernel<true><<<(unsigned)blocks, 128, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else
+    attn_tc_kernel<false><<<(unsigned)blocks, 128, SMEM_BYTES, st>>>(tq, tk, tv, p);
   return check_launch();
 }
 

@@ -87,7 +87,11 @@ __device__ __forceinline__ float gelu_erf(float x) {
 // One reciprocal and a degree-6 polynomial instead of a library erf: the GEMM
 // epilogue that applies it stays under the tensor-core time of its tile. The
 // result is rounded to bf16 right after, so the 3e-7 bound is far below the
-// output resolution; tests compare it with torch's erf GELU.
+// output resolution for x >= kGeluTail. Below it GELU is tiny and torch's own
+// value is 0.5 x (1 + erf) with erf rounded to fp32; callers recompute those
+// elements with gelu_erf (see gelu32), which also matches torch there.
+constexpr float kGeluTail = -3.0f;
+
 __device__ __forceinline__ float gelu_as(float x) {
   const float y = fminf(fabsf(x) * 0.70710678118654752440f, 1.0e4f);
   float q = fmaf(4.30638e-5f, y, 2.765672e-4f);
@@ -102,11 +106,30 @@ __device__ __forceinline__ float gelu_as(float x) {
   r = r * r;                      // r^8
   r = r * r;                      // r^16 = 1 - erf(y)
   const float h = 0.5f * x * r;  // 0.5 x (1 - erf(|x| / sqrt 2))
-  // Far in the negative tail GELU(x) = 0.5 x erfc(y) is tiny and the absolute
-  // 3e-7 bound is no longer small relative to it: use the library erfc there
-  // (x < -4 is rare after a LayerNorm, so the branch almost never diverges).
-  if (x < -4.0f) return 0.5f * x * erfcf(y);
   return x >= 0.f ? x - h : h;
+}
+
+// Kept out of line so that the compiler cannot if-convert the rare tail path
+// into every element of an unrolled epilogue loop.
+static __device__ __noinline__ float gelu_tail(float x) { return gelu_erf(x); }
+
+// GELU of 32 values in place: the polynomial form for all, then -- only when a
+// lane of the warp holds a tail value, which is rare after a LayerNorm -- the
+// library-erf form for the tail elements. All 32 lanes of the warp must call it.
+__device__ __forceinline__ void gelu32(float* v) {
+  bool tail = false;
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    x[i] = v[i];
+    tail |= (v[i] < kGeluTail);
+    v[i] = gelu_as(v[i]);
+  }
+  if (__any_sync(0xffffffffu, tail)) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (x[i] < kGeluTail) v[i] = gelu_tail(x[i]);
+  }
 }
 
 // ── shared-memory address helpers ────────────────────────────────────────────
@@ -147,23 +170,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait. Spins on the barrier phase until it completes, the shared
-// abort flag is raised by another thread, or ~kWaitCycles SM cycles pass. On a
-// timeout it records CK_ERR_TIMEOUT with a site code, raises the abort flag and
-// returns false; callers then leave their loops and the kernel exits cleanly.
+// Non-blocking probe of a barrier phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait. Polls the barrier phase (test_wait: the thread is never parked,
+// so a phase completed by a tcgen05.commit is seen at once) until it completes,
+// the shared abort flag is raised by another thread, or ~kWaitCycles SM cycles
+// pass. On a timeout it records CK_ERR_TIMEOUT with a site code, raises the
+// abort flag and returns false; callers then leave their loops and the kernel
+// exits cleanly.
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int site) {
-  if (mbar_try_wait(bar, parity)) return true;
-  long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (abort_flag != nullptr && *abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      set_status(CK_ERR_TIMEOUT, site, (int)parity);
-      if (abort_flag != nullptr) *abort_flag = 1;
-      return false;
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((n & 63u) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        set_status(CK_ERR_TIMEOUT, site, (int)parity);
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
     }
   }
 }

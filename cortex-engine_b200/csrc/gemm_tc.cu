@@ -85,8 +85,7 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, 
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = rbf(v[i]);  // linear output in bf16, as F.linear returns it
   if (EPI == CK_EPI_GELU) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
+    gelu32(v);
   } else if (EPI == CK_EPI_RESID || EPI == CK_EPI_BIAS) {
     if (m >= p.M) return;
     const __nv_bfloat16* src;
