@@ -35,6 +35,7 @@ SOURCES = [
     "attention_simt.cu",
     "capi.cu",
     "forward.cu",
+    "noalloc.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -110,6 +110,9 @@ _SIGS = {
     "ck_norm_linear": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _f32, _int, _vp, _int,
                               _int, _i64, _i64, _vp, _int, _vp, _i64, _i64, _vp, _i64, _vp,
                               _sz, _vp]),
+    "ck_norm_linear_static": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _f32, _int, _vp,
+                                     _int, _int, _i64, _i64, _vp, _int, _vp, _i64, _i64, _vp,
+                                     _i64, _vp]),
     "ck_attention": (_int, [ctypes.POINTER(AttentionArgs), _vp]),
     "ck_forward_workspace_bytes": (_sz, [ctypes.POINTER(Model), _i64, _i32]),
     "ck_forward": (_int, [ctypes.POINTER(Model), _vp, _vp, _vp, _vp, _int, _i64, _i32, _vp, _vp,

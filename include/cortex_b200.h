@@ -125,6 +125,25 @@ int ck_norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, 
                    const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* ck_norm_linear without a caller-provided workspace, for callers that cannot
+ * allocate device memory (a host runtime binding this ABI without a CUDA
+ * allocator of its own, or a serving loop that must not allocate once running).
+ * No counterpart in the reference: it is an addition of this library. The
+ * normalised activations go to a fixed 8 MiB array in device memory that the
+ * library defines (held by every GPU that loads it until the process exits):
+ * M*K elements of dtype must fit in CK_NORM_LINEAR_STATIC_SCRATCH_BYTES, or the
+ * call returns CK_ERR_INVALID_ARG without launching anything. All calls on a
+ * device share that array, so calls that overlap on the GPU race and must be
+ * serialised by the caller. The first call on each device looks up the array's
+ * address; make it before any stream capture. Same arguments and results as
+ * ck_norm_linear otherwise. */
+#define CK_NORM_LINEAR_STATIC_SCRATCH_BYTES (8u << 20)
+int ck_norm_linear_static(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                          const void* gamma, const void* beta, float eps, int norm_mode,
+                          const void* W, int w_dtype, int w_layout, int64_t N, int64_t ldw,
+                          const float* w_scale, int epi, const void* aux, int64_t ld_aux,
+                          int64_t aux_row_mod, void* Y, int64_t ldy, void* stream);
+
 /* ── 5. attention ───────────────────────────────────────────────────────────
  * softmax(q k^T * scale + mask) v per (batch b, head h), fp32 statistics.
  * Row r of (b, h) for tensor X in {q, k, v, o} lives at
