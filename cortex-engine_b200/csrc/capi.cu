@@ -23,9 +23,10 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
   if (w_dtype != dtype && w_dtype != CK_I8) return CK_ERR_UNSUPPORTED;
   if (w_dtype == CK_I8 && (w_scale == nullptr || w_layout != CK_W_NK)) return CK_ERR_INVALID_ARG;
   if (dtype == CK_BF16 && gemm_tc_supported(M, K, lda, w_dtype, w_layout, N, ldw, A, W, ldy, Y,
-                                            epi, aux, ld_aux))
+                                            epi, aux, ld_aux)) {
     return gemm_tc(A, M, K, lda, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux, ld_aux,
                    aux_row_mod, Y, ldy, st);
+  }
   return gemm_simt(A, dtype, M, K, lda, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux, ld_aux,
                    aux_row_mod, Y, ldy, st);
 }

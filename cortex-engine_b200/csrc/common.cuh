@@ -109,6 +109,54 @@ __device__ __forceinline__ float gelu_as(float x) {
   return x >= 0.f ? x - h : h;
 }
 
+// Paired fp32 arithmetic (sm_100: one instruction for two lanes of a .b64 pair).
+__device__ __forceinline__ unsigned long long f2pk(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2up(unsigned long long r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b,
+                                                    unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// gelu_as on two values with the polynomial and the squarings in paired fp32
+// instructions (same arithmetic, same rounding as gelu_as per element).
+__device__ __forceinline__ void gelu_as2(float& a, float& b) {
+  const float ya = fminf(fabsf(a) * 0.70710678118654752440f, 1.0e4f);
+  const float yb = fminf(fabsf(b) * 0.70710678118654752440f, 1.0e4f);
+  const unsigned long long y = f2pk(ya, yb);
+  unsigned long long q = ffma2(f2pk(4.30638e-5f, 4.30638e-5f), y,
+                               f2pk(2.765672e-4f, 2.765672e-4f));
+  q = ffma2(q, y, f2pk(1.520143e-4f, 1.520143e-4f));
+  q = ffma2(q, y, f2pk(9.2705272e-3f, 9.2705272e-3f));
+  q = ffma2(q, y, f2pk(4.22820123e-2f, 4.22820123e-2f));
+  q = ffma2(q, y, f2pk(7.05230784e-2f, 7.05230784e-2f));
+  q = ffma2(q, y, f2pk(1.0f, 1.0f));
+  float qa, qb;
+  f2up(q, qa, qb);
+  unsigned long long r = f2pk(__fdividef(1.0f, qa), __fdividef(1.0f, qb));
+  r = fmul2(r, r);
+  r = fmul2(r, r);
+  r = fmul2(r, r);
+  r = fmul2(r, r);
+  const unsigned long long h = fmul2(fmul2(f2pk(0.5f, 0.5f), f2pk(a, b)), r);
+  float ha, hb;
+  f2up(h, ha, hb);
+  a = a >= 0.f ? a - ha : ha;
+  b = b >= 0.f ? b - hb : hb;
+}
+
 // Kept out of line so that the compiler cannot if-convert the rare tail path
 // into every element of an unrolled epilogue loop.
 static __device__ __noinline__ float gelu_tail(float x) { return gelu_erf(x); }
@@ -118,17 +166,19 @@ static __device__ __noinline__ float gelu_tail(float x) { return gelu_erf(x); }
 // library-erf form for the tail elements. All 32 lanes of the warp must call it.
 __device__ __forceinline__ void gelu32(float* v) {
   bool tail = false;
-  float x[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    x[i] = v[i];
-    tail |= (v[i] < kGeluTail);
-    v[i] = gelu_as(v[i]);
-  }
+  for (int i = 0; i < 32; ++i) tail |= (v[i] < kGeluTail);
   if (__any_sync(0xffffffffu, tail)) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (x[i] < kGeluTail) v[i] = gelu_tail(x[i]);
+    for (int i = 0; i < 32; ++i) {
+      if (v[i] < kGeluTail)
+        v[i] = gelu_tail(v[i]);
+      else
+        v[i] = gelu_as(v[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
   }
 }
 

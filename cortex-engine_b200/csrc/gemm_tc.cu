@@ -23,16 +23,20 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "gemm_common.cuh"
 #include "kernels.h"
 
 namespace ck {
 
 namespace {
 
+using gemm::GemmArgs;
+using gemm::epilogue_math;
+
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int EPI_WARPS = 8;
-constexpr int STG_BYTES = 32 * 32 * 2;  // one 32x32 bf16 staging tile
+constexpr int STG_BOX = 32 * 64 * 2;  // one 32-row x 64-col bf16 store box (128B rows)
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
@@ -42,7 +46,9 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
   static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
-  static constexpr int EPI_SMEM = EPI_WARPS * 2 * STG_BYTES;  // double-buffered per warp
+  // per epilogue warp: one 32x64 store box, reused by its rounds of 64 columns
+  static constexpr int STG_WARP = STG_BOX;
+  static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
@@ -53,62 +59,6 @@ struct GemmCfg {
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
 };
-
-struct GemmArgs {
-  int M, N, K;
-  int num_m_tiles, num_n_tiles, num_k_blocks;
-  const __nv_bfloat16* aux;
-  int64_t ld_aux;
-  int64_t aux_row_mod;
-  const float* w_scale;
-  int scale_vec;  // w_scale is 16-byte aligned: vector loads
-};
-
-// Epilogue math for 32 consecutive columns n0.. of row m (v: fp32 accumulators).
-template <int EPI>
-__device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, float* v) {
-  const bool full = (n0 + 32 <= p.N);
-  if (p.w_scale != nullptr) {
-    if (full && p.scale_vec) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 s = __ldg(reinterpret_cast<const float4*>(p.w_scale + n0) + c);
-        v[4 * c] *= s.x;
-        v[4 * c + 1] *= s.y;
-        v[4 * c + 2] *= s.z;
-        v[4 * c + 3] *= s.w;
-      }
-    } else {
-      for (int i = 0; i < 32; ++i) v[i] *= (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = rbf(v[i]);  // linear output in bf16, as F.linear returns it
-  if (EPI == CK_EPI_GELU) {
-    gelu32(v);
-  } else if (EPI == CK_EPI_RESID || EPI == CK_EPI_BIAS) {
-    if (m >= p.M) return;
-    const __nv_bfloat16* src;
-    if (EPI == CK_EPI_RESID) {
-      const int64_t r = p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;
-      src = p.aux + r * p.ld_aux + n0;
-    } else {
-      src = p.aux + n0;
-    }
-    if (full) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float f[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(src) + c), f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[8 * c + j] = f[j] + v[8 * c + j];
-      }
-    } else {
-      for (int i = 0; i < 32; ++i)
-        if (n0 + i < p.N) v[i] = bf2f(src[i]) + v[i];
-    }
-  }
-}
 
 template <int BN, int WMODE, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
@@ -251,8 +201,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int half = e >> 2;
     const int row = quarter * 32 + lane;
-    uint8_t* stg = sStg + e * 2 * STG_BYTES;
-    int sbuf = 0;
+    uint8_t* stg = sStg + e * C::STG_WARP;
+    constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -262,33 +212,38 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
       tc_fence_after();
       const int m = mt * BM + row;
       const int m0 = mt * BM + quarter * 32;
+      const int col0 = half * (BN / 2);
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      // rounds of 64 columns: one batched TMEM read each (TMEM handed back to the
+      // MMA warp after the last read), epilogue math, a 128B-swizzled 32x64 box
+      // in smem and one TMA store per round
 #pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
-        const int col = half * (BN / 2) + c * 32;
-        const int n0 = nt * BN + col;
-        float v[32];
-        tmem_ld32(tbase + (uint32_t)col, v);
+      for (int r = 0; r < NCH / 2; ++r) {
+        float v[64];
+        tmem_ld32(tbase + (uint32_t)(col0 + r * 64), v);
+        tmem_ld32(tbase + (uint32_t)(col0 + r * 64 + 32), v + 32);
         tc_wait_ld();
-        if (n0 < p.N) epilogue_math<EPI>(p, m, n0, v);
-        // stage the 32x32 tile (64-byte rows, 64B swizzle) and store it with TMA
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-        uint8_t* buf = stg + sbuf * STG_BYTES;
+        if (r == NCH / 2 - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        const int nb = nt * BN + col0 + r * 64;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
-              pack8(v + 8 * q);
+        for (int c = 0; c < 2; ++c)
+          if (nb + c * 32 < p.N) epilogue_math<EPI>(p, m, nb + c * 32, v + 32 * c);
+        if (lane == 0) bulk_wait_read<0>();  // the previous store has read the box
+        __syncwarp();
+        uint8_t* box = stg;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<uint4*>(box + sw128_off(lane, q)) = pack8(v + 8 * q);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0 && n0 < p.N && m0 < p.M) {
-          tma_store_2d(&tmY, buf, n0, m0);
+        if (lane == 0 && m0 < p.M && nb < p.N) {
+          tma_store_2d(&tmY, box, nb, m0);
           bulk_commit();
         }
-        sbuf ^= 1;
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -407,7 +362,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   CUtensorMap ta, tb, ty;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
     return CK_ERR_INVALID_ARG;
-  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 32, 32, 64))
+  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 64, 32, 128))
     return CK_ERR_INVALID_ARG;
   bool ok;
   if (w_dtype == CK_I8) {

@@ -198,7 +198,8 @@ def _gemm_ref(x, w, w_scale=None, layout="nk"):
 
 @pytest.mark.parametrize("M,K,N", [(128, 64, 128), (256, 512, 512), (8192, 512, 1536),
                                    (8192, 512, 2048), (8192, 2048, 512), (33, 64, 97),
-                                   (300, 768, 2304), (2, 512, 512), (16384, 512, 1024)])
+                                   (300, 768, 2304), (2, 512, 512), (16384, 512, 1024),
+                                   (1000, 512, 320), (600, 100, 264), (256, 3072, 768)])
 def test_linear_tc_bf16(M, K, N):
     from cortex.kernels import _ops
 
