@@ -34,6 +34,8 @@ SOURCES = [
     "attention_tc.cu",
     "attention_simt.cu",
     "capi.cu",
+    "head.cu",
+    "fold.cu",
     "forward.cu",
     "noalloc.cu",
 ]

@@ -24,6 +24,8 @@ __device__ __forceinline__ float tof(T v) {
 
 template <typename T, int DHMAX>
 __global__ void __launch_bounds__(256) attn_simt_kernel(const ck_attention_args p, int num_q_tiles) {
+  grid_dep_wait();
+  grid_dep_launch();
   extern __shared__ float sm[];
   constexpr int LD = DHMAX + 1;
   float* Qs = sm;
@@ -152,8 +154,7 @@ int launch(const ck_attention_args& a, cudaStream_t st) {
   const int smem = (QROWS + 2 * KCH) * (DHMAX + 1) * (int)sizeof(float);
   if (!smem_attr_ready(reinterpret_cast<const void*>(attn_simt_kernel<T, DHMAX>), smem))
     return record_cuda_error();
-  attn_simt_kernel<T, DHMAX><<<(unsigned)blocks, 256, smem, st>>>(a, nqt);
-  return check_launch();
+  return launch_pdl(attn_simt_kernel<T, DHMAX>, dim3((unsigned)blocks), dim3(256), smem, st, a, nqt);
 }
 
 }  // namespace

@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(128, 2)
                    const __grid_constant__ CUtensorMap tmV, const TcAttnArgs p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // swizzled operand tiles need 1 KB alignment
+    grid_dep_wait();
     if (threadIdx.x == 0) set_status(CK_ERR_INVALID_ARG, 1024, (int)(smem_u32(smem_raw) & 1023u));
     return;
   }
@@ -142,25 +143,6 @@ __global__ void __launch_bounds__(128, 2)
   const int h = work % p.H;
   const int b = work / p.H;
 
-  int64_t key_row0;
-  int nk;
-  if (p.key_offsets != nullptr) {
-    key_row0 = p.key_offsets[b];
-    nk = p.key_offsets[b + 1] - p.key_offsets[b];
-  } else {
-    key_row0 = (int64_t)b * p.k_rows_per_b;
-    nk = p.n_keys;
-  }
-  const int64_t v_row0 = (p.key_offsets != nullptr) ? key_row0 : (int64_t)b * p.v_rows_per_b;
-  const int l0 = qt * QT;
-  const int l1 = min(l0 + QT, p.Lq);
-  const int q_row = (int)((int64_t)b * p.q_rows_per_b + (int64_t)h * p.q_rows_per_h + l0);
-  const int q_col = (int)((int64_t)h * p.q_col_per_h);
-  const int k_row_h = (int)(key_row0 + (int64_t)h * p.k_rows_per_h);
-  const int k_col = (int)((int64_t)h * p.k_col_per_h);
-  const int v_row_h = (int)(v_row0 + (int64_t)h * p.v_rows_per_h);
-  const int v_col = (int)((int64_t)h * p.v_col_per_h);
-
   if (tid == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
@@ -181,6 +163,27 @@ __global__ void __launch_bounds__(128, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();
+  grid_dep_launch();
+  int64_t key_row0;
+  int nk;
+  if (p.key_offsets != nullptr) {
+    key_row0 = p.key_offsets[b];
+    nk = p.key_offsets[b + 1] - p.key_offsets[b];
+  } else {
+    key_row0 = (int64_t)b * p.k_rows_per_b;
+    nk = p.n_keys;
+  }
+  const int64_t v_row0 = (p.key_offsets != nullptr) ? key_row0 : (int64_t)b * p.v_rows_per_b;
+  const int l0 = qt * QT;
+  const int l1 = min(l0 + QT, p.Lq);
+  const int q_row = (int)((int64_t)b * p.q_rows_per_b + (int64_t)h * p.q_rows_per_h + l0);
+  const int q_col = (int)((int64_t)h * p.q_col_per_h);
+  const int k_row_h = (int)(key_row0 + (int64_t)h * p.k_rows_per_h);
+  const int k_col = (int)((int64_t)h * p.k_col_per_h);
+  const int v_row_h = (int)(v_row0 + (int64_t)h * p.v_rows_per_h);
+  const int v_col = (int)((int64_t)h * p.v_col_per_h);
+
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_s = tmem_base;
   const uint32_t tmem_o = tmem_base + 128;
@@ -464,10 +467,10 @@ int attention_tc(const ck_attention_args& a, cudaStream_t st) {
   if (blocks <= 0) return CK_OK;
   if (blocks > INT32_MAX) return CK_ERR_INVALID_ARG;
   if (masked)
-    attn_tc_kernel<true><<<(unsigned)blocks, 128, SMEM_BYTES, st>>>(tq, tk, tv, p);
-  else
-    attn_tc_kernel<false><<<(unsigned)blocks, 128, SMEM_BYTES, st>>>(tq, tk, tv, p);
-  return check_launch();
+    return launch_pdl(attn_tc_kernel<true>, dim3((unsigned)blocks), dim3(128), SMEM_BYTES, st, tq,
+                      tk, tv, p);
+  return launch_pdl(attn_tc_kernel<false>, dim3((unsigned)blocks), dim3(128), SMEM_BYTES, st, tq,
+                    tk, tv, p);
 }
 
 }  // namespace ck

@@ -34,6 +34,22 @@ __device__ __forceinline__ void set_status(int code, int a = 0, int b = 0) {
   }
 }
 
+// ── programmatic dependent launch ────────────────────────────────────────────
+// Every kernel is launched with programmatic stream serialisation (launch_pdl
+// in kernels.h), so it may start while its stream predecessor is still
+// running. grid_dep_wait() blocks until the predecessor grid has completed and
+// its writes are visible; each kernel calls it before its first global-memory
+// read or write (setup that only touches shared memory, TMEM or kernel
+// parameters may come first). grid_dep_launch() lets the successor grid be
+// scheduled; kernels call it only after any blocking resource acquisition of
+// their own (TMEM allocation), so a successor that occupies an SM early can
+// never hold a resource a running CTA of this grid still has to acquire. Both
+// are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ── bf16 helpers ─────────────────────────────────────────────────────────────
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }

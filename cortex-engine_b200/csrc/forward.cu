@@ -7,9 +7,16 @@
 //   kv_proj         packed (E, 2D) keys|values                 (perceiver.py:67-69)
 //   cross attention varlen keys per sample, no padding          (perceiver.py:71-80)
 //   out_proj+resid  latents param broadcast as the residual      (perceiver.py:82)
-//   N x block       LN, qkv, attention, out+resid, LN, mlp0+GELU, mlp2+resid
-//   final LN + head LN (one pass), head q (batch-invariant), head kv_proj,
-//   2-query attention, out_proj D->1                           (cortex.py:29-53)
+//   N x block       LN, qkv, attention, out+resid, LN, mlp0+GELU, mlp2+resid; with
+//                   ck_norm_fold weights both LNs fold into qkv / mlp0 (their
+//                   producers emit row statistics) and no normalised copy exists
+//   final LN + head LN, head q, head kv_proj, 2-query attention, out_proj D->1
+//                   (cortex.py:29-53): bf16 models run it as one fused kernel on a
+//                   weight-only matrix built per forward (head.cu); otherwise
+//                   row_norm2, two linears, attention and a GEMV
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,8 +38,28 @@ size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
   size_t counts, offsets, dest, emax, packws, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
-      total;
+      qall, stats, total;
 };
+
+// Per-row LayerNorm statistics segments of a (., D) residual GEMM output.
+int64_t stats_segments(int64_t D) {
+  const int64_t sw = gemm_tc_block_n(D) / 2;
+  return (D + sw - 1) / sw;
+}
+
+// LayerNorm folding into qkv_proj / mlp.0 (ck_norm_fold); CK_NORM_FOLD=0 in the
+// environment keeps the separate norm kernels.
+bool norm_fold_enabled() {
+  const char* v = std::getenv("CK_NORM_FOLD");
+  return v == nullptr || std::strcmp(v, "0") != 0;
+}
+
+// The fused behaviour head (head.cu) runs whenever the model qualifies;
+// CK_HEAD_FUSED=0 in the environment selects the composed head instead.
+bool use_fused_head(const ck_model* m) {
+  const char* v = std::getenv("CK_HEAD_FUSED");
+  return (v == nullptr || std::strcmp(v, "0") != 0) && head_fused_supported(m);
+}
 
 Layout plan(const ck_model* m, int64_t E, int32_t B) {
   const size_t es = m->dtype == CK_F32 ? 4 : 2;
@@ -61,6 +88,8 @@ Layout plan(const ck_model* m, int64_t E, int32_t B) {
   o.hbuf = take(BL * (size_t)m->mlp_hidden * es);
   o.qh = take((size_t)m->behavior_dim * D * es);
   o.oh = take((size_t)B * m->behavior_dim * D * es);
+  o.qall = take(use_fused_head(m) ? head_qall_bytes(m) : 1);
+  o.stats = take((size_t)stats_segments(D) * BL * sizeof(float2));
   o.total = p;
   return o;
 }
@@ -74,6 +103,41 @@ int lin(const ck_model* m, const void* A, int64_t M, int64_t K, int64_t lda,
   if (wd != m->dtype && wd != CK_I8) return CK_ERR_UNSUPPORTED;
   return linear_dispatch(A, m->dtype, M, K, lda, w.w, wd, CK_W_NK, N, K, w.scale, epi, aux,
                          ld_aux, mod, Y, ldy, st);
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Can this residual linear run on the tensor-core GEMM (and so emit statistics)?
+bool resid_tc_ok(const ck_model* m, const ck_linear_weight& w, int64_t M, int64_t K, int64_t N,
+                 const void* A, const void* aux, int64_t ld_aux, const void* Y) {
+  if (m->dtype != CK_BF16 || w.w == nullptr || w.bias != nullptr) return false;
+  if (w.dtype != CK_BF16 && !(w.dtype == CK_I8 && w.scale != nullptr)) return false;
+  return gemm_tc_supported(M, K, K, w.dtype, CK_W_NK, N, K, A, w.w, N, Y, CK_EPI_RESID, aux,
+                           ld_aux);
+}
+
+// Can this norm + linear pair run folded?
+bool fold_tc_ok(const ck_model* m, const ck_norm_fold& f, const ck_linear_weight& w, int64_t M,
+                int64_t K, int64_t N, const void* A, int epi, const void* Y) {
+  if (!norm_fold_enabled() || m->dtype != CK_BF16) return false;
+  if (f.w == nullptr || f.colsum == nullptr || f.bias == nullptr || w.bias != nullptr) return false;
+  if (!al16(f.colsum) || !al16(f.bias)) return false;
+  return gemm_tc_supported(M, K, K, CK_BF16, CK_W_NK, N, K, A, f.w, N, Y, epi, nullptr, 0);
+}
+
+int lin_stats(const ck_model* m, const void* A, int64_t M, int64_t K, const ck_linear_weight& w,
+              int64_t N, const void* aux, int64_t ld_aux, int64_t mod, void* Y, void* stats,
+              cudaStream_t st) {
+  GemmFusion fz = {stats, nullptr, 0, 0.f, nullptr, nullptr};
+  return gemm_tc(A, M, K, K, w.w, w.dtype, CK_W_NK, N, K, w.scale, CK_EPI_RESID, aux, ld_aux, mod,
+                 Y, N, st, &fz);
+}
+
+int lin_folded(const void* A, int64_t M, int64_t K, const ck_norm_fold& f, int64_t N, int epi,
+               const void* stats, void* Y, cudaStream_t st) {
+  GemmFusion fz = {nullptr, stats, gemm_tc_block_n(K) / 2, 1e-5f, f.colsum, f.bias};
+  return gemm_tc(A, M, K, K, f.w, CK_BF16, CK_W_NK, N, K, nullptr, epi, nullptr, 0, 0, Y, N, st,
+                 &fz);
 }
 
 ck_attention_args attn_base(const ck_model* m) {
@@ -135,6 +199,8 @@ extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, co
   CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
                   CK_NORM_LAYER, P(lay.xq), D, st));
   CK_TRY(lin(m, P(lay.xq), L, D, D, m->cross_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qc), D, st));
+  const bool fused_head = use_fused_head(m);
+  if (fused_head) CK_TRY(head_prep(m, P(lay.qall), st));
   // 4. packed keys|values
   if (E > 0)
     CK_TRY(lin(m, P(lay.xkv), E, Din, Din, m->cross_kv, 2 * D, CK_EPI_STORE, nullptr, 0, 0,
@@ -167,17 +233,43 @@ extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, co
     a.scale = 1.0f / sqrtf((float)Dhc);
     CK_TRY(attention_dispatch(a, st));
   }
+  // Which norms fold into their linears: a folded consumer needs its producer
+  // (the residual GEMM before it) on the tensor-core path to emit statistics.
+  const int64_t Hm = m->mlp_hidden;
+  void* stats = P(lay.stats);
+  auto fold_qkv = [&](int i) {
+    if (i >= m->num_layers) return false;
+    const bool prod = i == 0 ? resid_tc_ok(m, m->cross_out, BL, D, D, P(lay.att), m->latents, D,
+                                           P(lay.lat))
+                             : resid_tc_ok(m, m->blocks[i - 1].mlp2, BL, Hm, D, P(lay.hbuf),
+                                           P(lay.lat), D, P(lay.lat));
+    return prod && fold_tc_ok(m, m->blocks[i].qkv_fold, m->blocks[i].qkv, BL, D, 3 * D, P(lay.lat),
+                              CK_EPI_STORE, P(lay.qkv));
+  };
+  auto fold_mlp0 = [&](int i) {
+    return resid_tc_ok(m, m->blocks[i].out, BL, D, D, P(lay.att), P(lay.lat), D, P(lay.lat)) &&
+           fold_tc_ok(m, m->blocks[i].mlp0_fold, m->blocks[i].mlp0, BL, D, Hm, P(lay.lat),
+                      CK_EPI_GELU, P(lay.hbuf));
+  };
   // 6. out_proj + broadcast latent residual
-  CK_TRY(lin(m, P(lay.att), BL, D, D, m->cross_out, D, CK_EPI_RESID, m->latents, D, L, P(lay.lat),
-             D, st));
+  if (fold_qkv(0))
+    CK_TRY(lin_stats(m, P(lay.att), BL, D, m->cross_out, D, m->latents, D, L, P(lay.lat), stats,
+                     st));
+  else
+    CK_TRY(lin(m, P(lay.att), BL, D, D, m->cross_out, D, CK_EPI_RESID, m->latents, D, L,
+               P(lay.lat), D, st));
   // 7. self-attention blocks
   const size_t es_b = m->dtype == CK_F32 ? 4 : 2;
   for (int i = 0; i < m->num_layers; ++i) {
     const ck_block_weights& w = m->blocks[i];
-    CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b, kLnEps,
-                    CK_NORM_LAYER, P(lay.x), D, st));
-    CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
-               3 * D, st));
+    if (fold_qkv(i)) {
+      CK_TRY(lin_folded(P(lay.lat), BL, D, w.qkv_fold, 3 * D, CK_EPI_STORE, stats, P(lay.qkv), st));
+    } else {
+      CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b,
+                      kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
+      CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
+                 3 * D, st));
+    }
     ck_attention_args a = attn_base(m);
     a.B = B;
     a.H = (int32_t)H;
@@ -205,14 +297,27 @@ extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, co
     a.o_col_per_h = Dh;
     a.scale = 1.0f / sqrtf((float)Dh);
     CK_TRY(attention_dispatch(a, st));
-    CK_TRY(lin(m, P(lay.att), BL, D, D, w.out, D, CK_EPI_RESID, P(lay.lat), D, 0, P(lay.lat), D,
-               st));
-    CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_mlp_w, w.norm_mlp_b, kLnEps,
-                    CK_NORM_LAYER, P(lay.x), D, st));
-    CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, m->mlp_hidden, CK_EPI_GELU, nullptr, 0, 0,
-               P(lay.hbuf), m->mlp_hidden, st));
-    CK_TRY(lin(m, P(lay.hbuf), BL, m->mlp_hidden, m->mlp_hidden, w.mlp2, D, CK_EPI_RESID,
-               P(lay.lat), D, 0, P(lay.lat), D, st));
+    if (fold_mlp0(i)) {
+      CK_TRY(lin_stats(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat), stats, st));
+      CK_TRY(lin_folded(P(lay.lat), BL, D, w.mlp0_fold, Hm, CK_EPI_GELU, stats, P(lay.hbuf), st));
+    } else {
+      CK_TRY(lin(m, P(lay.att), BL, D, D, w.out, D, CK_EPI_RESID, P(lay.lat), D, 0, P(lay.lat), D,
+                 st));
+      CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_mlp_w, w.norm_mlp_b,
+                      kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
+      CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, Hm, CK_EPI_GELU, nullptr, 0, 0, P(lay.hbuf), Hm,
+                 st));
+    }
+    if (fold_qkv(i + 1))
+      CK_TRY(lin_stats(m, P(lay.hbuf), BL, Hm, w.mlp2, D, P(lay.lat), D, 0, P(lay.lat), stats, st));
+    else
+      CK_TRY(lin(m, P(lay.hbuf), BL, Hm, Hm, w.mlp2, D, CK_EPI_RESID, P(lay.lat), D, 0,
+                 P(lay.lat), D, st));
+  }
+  // 8-9. final_norm, head norm and the behaviour head in one kernel
+  if (fused_head) {
+    CK_TRY(head_fused(m, P(lay.lat), B, P(lay.qall), out, st));
+    return CK_OK;
   }
   // 8. final_norm then the head's norm
   CK_TRY(row_norm2(P(lay.lat), m->dtype, BL, (int32_t)D, D, m->final_norm_w, m->final_norm_b,

@@ -1,6 +1,6 @@
-// Pieces shared by the 1-SM and 2-SM tcgen05 GEMM kernels: the argument block
-// and the epilogue arithmetic (per-channel INT8 scale, rounding of the linear
-// output to bf16 as torch's F.linear returns it, then GELU / residual / bias).
+// Pieces of the tcgen05 GEMM: the argument block and the epilogue arithmetic
+// (folded LayerNorm, per-channel INT8 scale, rounding of the linear output to
+// bf16 as torch's F.linear returns it, then GELU / residual / bias).
 #pragma once
 
 #include "common.cuh"
@@ -16,12 +16,74 @@ struct GemmArgs {
   int64_t aux_row_mod;
   const float* w_scale;
   int scale_vec;  // w_scale is 16-byte aligned: vector loads
+  // Row statistics written by a residual epilogue (FUSE_STATS): for every row m
+  // and every stats_sw-wide column segment s, stats_out[s * M + m] = (mean,
+  // sum of squared deviations) of the segment's bf16 outputs.
+  float2* stats_out;
+  int stats_sw;
+  // LayerNorm folded into this GEMM (FUSE_NORM): A holds the raw rows, the
+  // weight is W * gamma, and the epilogue applies
+  //   y = rstd * (acc - mean * fold_cs[n]) + fold_bw[n]
+  // with mean / rstd combined from the producer's segment statistics.
+  const float2* stats_in;
+  int stats_in_sw, stats_in_nseg;
+  float norm_eps;
+  const float* fold_cs;
+  const float* fold_bw;
 };
 
+enum Fuse { FUSE_NONE = 0, FUSE_NORM = 1, FUSE_STATS = 2 };
+
+// Producer statistics of one row (up to 8 segments), fetched ahead of use.
+struct StatsRow {
+  float2 seg[8];
+};
+
+__device__ __forceinline__ StatsRow load_stats(const GemmArgs& p, int m) {
+  StatsRow r;
+#pragma unroll
+  for (int s = 0; s < 8; ++s)
+    r.seg[s] = (m < p.M && s < p.stats_in_nseg) ? p.stats_in[(int64_t)s * p.M + m]
+                                                : make_float2(0.f, 0.f);
+  return r;
+}
+
+// Mean and rstd of the row from its per-segment (mean, M2) pairs (Chan et
+// al.'s pairwise combination).
+__device__ __forceinline__ void combine_stats(const GemmArgs& p, const StatsRow& r, float& mean,
+                                              float& rstd) {
+  float mu = 0.f;
+#pragma unroll
+  for (int s = 0; s < 8; ++s)
+    if (s < p.stats_in_nseg) mu += (float)min(p.stats_in_sw, p.K - s * p.stats_in_sw) * r.seg[s].x;
+  mu /= (float)p.K;
+  float m2 = 0.f;
+#pragma unroll
+  for (int s = 0; s < 8; ++s)
+    if (s < p.stats_in_nseg) {
+      const float d = r.seg[s].x - mu;
+      m2 += r.seg[s].y + (float)min(p.stats_in_sw, p.K - s * p.stats_in_sw) * d * d;
+    }
+  mean = mu;
+  rstd = 1.0f / sqrtf(m2 / (float)p.K + p.norm_eps);
+}
+
 // Epilogue math for 32 consecutive columns n0.. of row m (v: fp32 accumulators).
-template <int EPI>
-__device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, float* v) {
+// FUSE_NORM applies the folded LayerNorm with the row's (mean, rstd) first.
+// fold: the (colsum, bias) pairs of columns n0..n0+31 in shared memory.
+template <int EPI, int FUSE = FUSE_NONE>
+__device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, float* v,
+                                              float mean = 0.f, float rstd = 0.f,
+                                              const float2* fold = nullptr) {
   const bool full = (n0 + 32 <= p.N);
+  if (FUSE == FUSE_NORM) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {  // columns beyond N hold (0, 0)
+      const float4 f = reinterpret_cast<const float4*>(fold)[c];
+      v[2 * c + 0] = fmaf(rstd, fmaf(-mean, f.x, v[2 * c + 0]), f.y);
+      v[2 * c + 1] = fmaf(rstd, fmaf(-mean, f.z, v[2 * c + 1]), f.w);
+    }
+  }
   if (p.w_scale != nullptr) {
     if (full && p.scale_vec) {
 #pragma unroll
@@ -33,6 +95,7 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, 
         v[4 * c + 3] *= s.w;
       }
     } else {
+#pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
     }
   }
@@ -58,6 +121,7 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, 
         for (int j = 0; j < 8; ++j) v[8 * c + j] = f[j] + v[8 * c + j];
       }
     } else {
+#pragma unroll
       for (int i = 0; i < 32; ++i)
         if (n0 + i < p.N) v[i] = bf2f(src[i]) + v[i];
     }

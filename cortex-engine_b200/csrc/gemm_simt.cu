@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(
     const T* A, int64_t M, int64_t K, int64_t lda, const WT* W, int w_layout, int64_t N,
     int64_t ldw, const float* w_scale, int epi, const T* aux, int64_t ld_aux, int64_t aux_row_mod,
     T* Y, int64_t ldy) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ float As[TK][TM + 4];
   __shared__ float Ws[TK][TN + 4];
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(256) gemv_rows_kernel(
     const T* A, int64_t M, int64_t K, int64_t lda, const WT* W, int w_layout, int64_t N,
     int64_t ldw, const float* w_scale, int epi, const T* aux, int64_t ld_aux, int64_t aux_row_mod,
     T* Y, int64_t ldy) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t m = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (m >= M) return;
@@ -152,18 +156,16 @@ int launch(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int 
   if (N <= 8) {
     const int64_t blocks = (M * 32 + 255) / 256;
     if (blocks > INT32_MAX) return CK_ERR_INVALID_ARG;
-    gemv_rows_kernel<T, WT, 8><<<(unsigned)blocks, 256, 0, st>>>(
+    return launch_pdl(gemv_rows_kernel<T, WT, 8>, dim3((unsigned)blocks), dim3(256), 0, st,
         reinterpret_cast<const T*>(A), M, K, lda, reinterpret_cast<const WT*>(W), w_layout, N,
         ldw, w_scale, epi, reinterpret_cast<const T*>(aux), ld_aux, mod, reinterpret_cast<T*>(Y),
         ldy);
-    return check_launch();
   }
   dim3 grid((unsigned)((N + TN - 1) / TN), (unsigned)((M + TM - 1) / TM));
   if (grid.y > 65535) return CK_ERR_INVALID_ARG;
-  gemm_simt_kernel<T, WT><<<grid, 256, 0, st>>>(
+  return launch_pdl(gemm_simt_kernel<T, WT>, dim3(grid), dim3(256), 0, st,
       reinterpret_cast<const T*>(A), M, K, lda, reinterpret_cast<const WT*>(W), w_layout, N, ldw,
       w_scale, epi, reinterpret_cast<const T*>(aux), ld_aux, mod, reinterpret_cast<T*>(Y), ldy);
-  return check_launch();
 }
 
 }  // namespace

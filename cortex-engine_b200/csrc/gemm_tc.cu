@@ -40,7 +40,7 @@ constexpr int STG_BOX = 32 * 64 * 2;  // one 32-row x 64-col bf16 store box (128
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
-template <int BN, int WMODE>
+template <int BN, int WMODE, int FUSE = 0>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;                        // 16 KB
   static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
@@ -50,21 +50,24 @@ struct GemmCfg {
   static constexpr int STG_WARP = STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM;
+  // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
+  // one buffer per TMEM accumulator, so the epilogue reads them at smem latency
+  static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * (BN / 2) * 8 : 0;
+  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
   static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
   static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + BAR_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
 };
 
-template <int BN, int WMODE, int EPI>
-__global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
+template <int BN, int WMODE, int EPI, int FUSE>
+__global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmY, const GemmArgs p) {
-  using C = GemmCfg<BN, WMODE>;
+  using C = GemmCfg<BN, WMODE, FUSE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -72,7 +75,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
   uint8_t* sB = sA + C::STAGES * C::A_BYTES;
   uint8_t* sB8 = sB + C::STAGES * C::B_BYTES;
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
-  uint8_t* sBar = sStg + C::EPI_SMEM;
+  float2* sFold = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);  // [8][2][BN/2] (FUSE_NORM)
+  uint8_t* sBar = sStg + C::EPI_SMEM + C::FOLD_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
   uint64_t* conv = empty + C::STAGES;
@@ -114,6 +118,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == 0) {
     // ── TMA producer ──
@@ -205,12 +211,47 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
     constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0;
     uint32_t acc_phase = 0;
+    // Folded LayerNorm (FUSE_NORM): the next tile's row statistics and column
+    // terms are fetched while the current tile is processed (registers for the
+    // statistics, this warp's sFold[e][acc ^ 1] for its columns), so their
+    // global latency stays off the per-tile chain. Warp-private: no barrier.
+    constexpr int FPL = (BN / 2) / 32;  // fold columns per lane
+    float2* wfold = sFold + e * BN;     // [2][BN / 2]
+    gemm::StatsRow srow;
+    float2 fold_next[FPL];
+    auto fetch_fold = [&](int t) {
+#pragma unroll
+      for (int j = 0; j < FPL; ++j) {
+        const int n = (t / p.num_m_tiles) * BN + half * (BN / 2) + j * 32 + lane;
+        fold_next[j] = n < p.N ? make_float2(__ldg(p.fold_cs + n), __ldg(p.fold_bw + n))
+                               : make_float2(0.f, 0.f);
+      }
+    };
+    if (FUSE == gemm::FUSE_NORM && (int)blockIdx.x < num_tiles) {
+      srow = gemm::load_stats(p, (blockIdx.x % p.num_m_tiles) * BM + row);
+      fetch_fold(blockIdx.x);
+#pragma unroll
+      for (int j = 0; j < FPL; ++j) wfold[j * 32 + lane] = fold_next[j];
+    }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int mt = tile % p.num_m_tiles;
       const int nt = tile / p.num_m_tiles;
+      float nmean = 0.f, nrstd = 0.f;  // folded LayerNorm of this row (FUSE_NORM)
+      if (FUSE == gemm::FUSE_NORM) {
+        gemm::combine_stats(p, srow, nmean, nrstd);
+        __syncwarp();  // this tile's fold terms are in wfold[acc]
+        const int tn = tile + gridDim.x;
+        if (tn < num_tiles) {
+          srow = gemm::load_stats(p, (tn % p.num_m_tiles) * BM + row);
+          fetch_fold(tn);
+        }
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
+      __syncwarp();
       tc_fence_after();
       const int m = mt * BM + row;
+      float st_shift = 0.f, st_s1 = 0.f, st_s2 = 0.f;  // segment statistics (FUSE_STATS)
+      int st_cnt = 0;
       const int m0 = mt * BM + quarter * 32;
       const int col0 = half * (BN / 2);
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
@@ -230,7 +271,40 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
         const int nb = nt * BN + col0 + r * 64;
 #pragma unroll
         for (int c = 0; c < 2; ++c)
-          if (nb + c * 32 < p.N) epilogue_math<EPI>(p, m, nb + c * 32, v + 32 * c);
+          if (nb + c * 32 < p.N)
+            epilogue_math<EPI, FUSE>(p, m, nb + c * 32, v + 32 * c, nmean, nrstd,
+                                     wfold + acc * (BN / 2) + r * 64 + c * 32);
+        if (FUSE == gemm::FUSE_STATS && nb < p.N) {
+          // statistics of the values as stored (bf16), shifted by the segment's
+          // first value so the sum of squares does not cancel
+#pragma unroll
+          for (int i = 0; i < 64; ++i) v[i] = rbf(v[i]);
+          if (r == 0) st_shift = v[0];
+          if (nb + 64 <= p.N) {
+            float s1a = 0.f, s1b = 0.f, s2a = 0.f, s2b = 0.f;
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) {
+              const float d0 = v[i] - st_shift, d1 = v[i + 1] - st_shift;
+              s1a += d0;
+              s1b += d1;
+              s2a = fmaf(d0, d0, s2a);
+              s2b = fmaf(d1, d1, s2b);
+            }
+            st_s1 += s1a + s1b;
+            st_s2 += s2a + s2b;
+            st_cnt += 64;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              if (nb + i < p.N) {
+                const float d = v[i] - st_shift;
+                st_s1 += d;
+                st_s2 = fmaf(d, d, st_s2);
+                ++st_cnt;
+              }
+            }
+          }
+        }
         if (lane == 0) bulk_wait_read<0>();  // the previous store has read the box
         __syncwarp();
         uint8_t* box = stg;
@@ -243,6 +317,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
           tma_store_2d(&tmY, box, nb, m0);
           bulk_commit();
         }
+      }
+      if (FUSE == gemm::FUSE_NORM && tile + (int)gridDim.x < num_tiles) {
+#pragma unroll
+        for (int j = 0; j < FPL; ++j) wfold[(acc ^ 1) * (BN / 2) + j * 32 + lane] = fold_next[j];
+      }
+      if (FUSE == gemm::FUSE_STATS && m < p.M && st_cnt > 0) {
+        const int seg = (nt * BN + col0) / p.stats_sw;
+        const float mu = st_s1 / (float)st_cnt;
+        p.stats_out[(int64_t)seg * p.M + m] =
+            make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
@@ -291,28 +375,43 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE>::NUM_THREADS, 1)
   }
 }
 
-template <int BN, int WMODE, int EPI>
+template <int BN, int WMODE, int EPI, int FUSE>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
                 const GemmArgs& a, cudaStream_t st) {
-  using C = GemmCfg<BN, WMODE>;
+  using C = GemmCfg<BN, WMODE, FUSE>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
-  auto kern = gemm_tc_kernel<BN, WMODE, EPI>;
+  auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
     return record_cuda_error();
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(ta, tb, ty, a);
-  return check_launch();
+  return launch_pdl(kern, dim3(grid), dim3(C::NUM_THREADS), C::SMEM_BYTES, st, ta, tb, ty, a);
 }
 
+// Instantiated combinations: a folded LayerNorm feeds only bf16 (N, K) weights
+// with a store or GELU epilogue; statistics come only from residual epilogues.
 template <int BN, int WMODE>
-int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
-                 const GemmArgs& a, cudaStream_t st) {
+int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb,
+                 const CUtensorMap& ty, const GemmArgs& a, cudaStream_t st) {
+  using gemm::FUSE_NONE;
+  using gemm::FUSE_NORM;
+  using gemm::FUSE_STATS;
+  if (fuse == FUSE_NORM) {
+    if constexpr (WMODE == W_BF16_NK) {
+      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NORM>(ta, tb, ty, a, st);
+      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NORM>(ta, tb, ty, a, st);
+    }
+    return CK_ERR_UNSUPPORTED;
+  }
+  if (fuse == FUSE_STATS) {
+    if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty, a, st);
+    return CK_ERR_UNSUPPORTED;
+  }
   switch (epi) {
-    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE>(ta, tb, ty, a, st);
-    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU>(ta, tb, ty, a, st);
-    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID>(ta, tb, ty, a, st);
-    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS>(ta, tb, ty, a, st);
+    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE>(ta, tb, ty, a, st);
+    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE>(ta, tb, ty, a, st);
+    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_NONE>(ta, tb, ty, a, st);
+    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS, FUSE_NONE>(ta, tb, ty, a, st);
   }
   return CK_ERR_INVALID_ARG;
 }
@@ -341,10 +440,13 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
   return true;
 }
 
+int gemm_tc_block_n(int64_t N) { return (N % 256 == 0 || N > 256) ? 256 : 128; }
+
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
-            int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st) {
-  const int BN = (N % 256 == 0 || N > 256) ? 256 : 128;
+            int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st,
+            const GemmFusion* fz) {
+  const int BN = gemm_tc_block_n(N);
   GemmArgs a;
   a.M = (int)M;
   a.N = (int)N;
@@ -358,6 +460,34 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.w_scale = (w_dtype == CK_I8) ? w_scale : nullptr;
   if (w_dtype == CK_I8 && w_scale == nullptr) return CK_ERR_INVALID_ARG;
   a.scale_vec = (reinterpret_cast<uintptr_t>(w_scale) & 15u) == 0;
+  a.stats_out = nullptr;
+  a.stats_sw = BN / 2;
+  a.stats_in = nullptr;
+  a.stats_in_sw = 0;
+  a.stats_in_nseg = 0;
+  a.norm_eps = 0.f;
+  a.fold_cs = nullptr;
+  a.fold_bw = nullptr;
+  int fuse = gemm::FUSE_NONE;
+  if (fz != nullptr && fz->stats_out != nullptr) {
+    if (epi != CK_EPI_RESID) return CK_ERR_UNSUPPORTED;
+    a.stats_out = reinterpret_cast<float2*>(fz->stats_out);
+    fuse = gemm::FUSE_STATS;
+  } else if (fz != nullptr && fz->stats_in != nullptr) {
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (w_dtype != CK_BF16 || w_layout != CK_W_NK || (epi != CK_EPI_STORE && epi != CK_EPI_GELU) ||
+        fz->stats_in_sw <= 0 || fz->fold_cs == nullptr || fz->fold_bw == nullptr ||
+        !al16(fz->fold_cs) || !al16(fz->fold_bw))
+      return CK_ERR_UNSUPPORTED;
+    a.stats_in = reinterpret_cast<const float2*>(fz->stats_in);
+    a.stats_in_sw = fz->stats_in_sw;
+    a.stats_in_nseg = (int)((K + fz->stats_in_sw - 1) / fz->stats_in_sw);
+    if (a.stats_in_nseg > 8) return CK_ERR_UNSUPPORTED;
+    a.norm_eps = fz->eps;
+    a.fold_cs = fz->fold_cs;
+    a.fold_bw = fz->fold_bw;
+    fuse = gemm::FUSE_NORM;
+  }
 
   CUtensorMap ta, tb, ty;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
@@ -375,13 +505,13 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   if (!ok) return CK_ERR_INVALID_ARG;
 
   if (BN == 256) {
-    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, ta, tb, ty, a, st);
-    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, ta, tb, ty, a, st);
-    return dispatch_epi<256, W_BF16_KN>(epi, ta, tb, ty, a, st);
+    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, fuse, ta, tb, ty, a, st);
+    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, fuse, ta, tb, ty, a, st);
+    return dispatch_epi<256, W_BF16_KN>(epi, fuse, ta, tb, ty, a, st);
   }
-  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, ta, tb, ty, a, st);
-  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, ta, tb, ty, a, st);
-  return dispatch_epi<128, W_BF16_KN>(epi, ta, tb, ty, a, st);
+  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, fuse, ta, tb, ty, a, st);
+  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, fuse, ta, tb, ty, a, st);
+  return dispatch_epi<128, W_BF16_KN>(epi, fuse, ta, tb, ty, a, st);
 }
 
 }  // namespace ck

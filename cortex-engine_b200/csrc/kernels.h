@@ -14,6 +14,28 @@ int num_sms();
 int record_cuda_error();  // stores cudaGetLastError() and returns CK_ERR_CUDA
 int check_launch();       // CK_OK or record_cuda_error()
 bool smem_attr_ready(const void* kernel, int bytes);  // per device, once
+bool pdl_enabled();       // CK_PDL=0 in the environment turns programmatic launch off
+int finish_launch(cudaError_t e);  // counts the launch; CK_OK or CK_ERR_CUDA
+
+// Launch a kernel with programmatic stream serialisation: the grid may be
+// scheduled while the previous kernel in the stream is finishing, and waits
+// for it inside the kernel (grid_dep_wait in common.cuh). Captured into a CUDA
+// graph this becomes a programmatic edge.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return finish_launch(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
+}
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                   uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t box_inner,
@@ -23,9 +45,25 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
 bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_layout, int64_t N,
                        int64_t ldw, const void* A, const void* W, int64_t ldy, const void* Y,
                        int epi, const void* aux, int64_t ld_aux);
+// Optional epilogue fusions of the tcgen05 GEMM (see gemm_common.cuh):
+//   stats_out  residual epilogue also writes per-row, per-segment (mean, M2)
+//              of its output, segment width gemm_tc_block_n(N) / 2
+//   stats_in   LayerNorm folded into this GEMM: A is the raw residual, W is
+//              W * gamma, fold_cs[n] = sum_k W[n,k] * gamma[k] (as stored),
+//              fold_bw[n] = sum_k W[n,k] * beta[k]
+struct GemmFusion {
+  void* stats_out;
+  const void* stats_in;
+  int stats_in_sw;
+  float eps;
+  const float* fold_cs;
+  const float* fold_bw;
+};
+int gemm_tc_block_n(int64_t N);
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
-            int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st);
+            int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st,
+            const GemmFusion* fz = nullptr);
 
 // CUDA-core GEMM, fp32 accumulate (gemm_simt.cu)
 int gemm_simt(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
@@ -62,10 +100,13 @@ int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
              const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
              cudaStream_t st);
 
-// behaviour head tail: attention of `nq` learned queries over L latents per
-// sample followed by out_proj (D -> 1) (head.cu)
-int head_attention_out(const void* q, const void* kv, int dtype, int32_t B, int32_t L, int32_t nq,
-                       int32_t H, int32_t Dh, const void* w_out, int w_dtype,
-                       const float* w_scale, const void* bias, void* y, cudaStream_t st);
+// behaviour head in algebraic form (head.cu): head_prep builds the weight-only
+// (NT, D) matrix once per forward, head_fused runs both LayerNorms, the
+// projection against it, the per-head softmax and out_proj in one kernel.
+bool head_fused_supported(const ck_model* m);
+size_t head_qall_bytes(const ck_model* m);
+int head_prep(const ck_model* m, void* qall, cudaStream_t st);
+int head_fused(const ck_model* m, const void* lat, int32_t B, const void* qall, void* out,
+               cudaStream_t st);
 
 }  // namespace ck

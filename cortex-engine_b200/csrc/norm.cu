@@ -91,6 +91,8 @@ template <typename T, int VEC, int MAXV>
 __global__ void row_norm_kernel(const T* x, int64_t M, int D, int64_t ldx, const T* g1,
                                 const T* b1, const T* g2, const T* b2, float eps, int mode,
                                 int two, T* y, int64_t ldy) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -151,6 +153,113 @@ __global__ void row_norm_kernel(const T* x, int64_t M, int D, int64_t ldx, const
   }
 }
 
+// bf16 LayerNorm fast path: G lanes per row (32 / G rows per warp), MAXV
+// 16-byte vectors per lane, gamma / beta as 16-byte vectors. Same two-pass
+// statistics as row_norm_kernel; TWO applies a second LayerNorm after rounding.
+template <int MAXV, int G, bool TWO>
+__global__ void __launch_bounds__(256) layer_norm_bf16_kernel(
+    const __nv_bfloat16* x, int64_t M, int D, int64_t ldx, const __nv_bfloat16* g1,
+    const __nv_bfloat16* b1, const __nv_bfloat16* g2, const __nv_bfloat16* b2, float eps,
+    __nv_bfloat16* y, int64_t ldy) {
+  grid_dep_wait();
+  grid_dep_launch();
+  constexpr int RPW = 32 / G;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % G;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nvec = D / 8;
+  for (int64_t base = warp * RPW; base < M; base += nwarps * RPW) {
+    const int64_t r = base + lane / G;
+    const bool live = r < M;
+    float v[MAXV][8];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c = sub + G * i;
+      if (live && c < nvec) {
+        unpack8(reinterpret_cast<const uint4*>(x + r * ldx)[c], v[i]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int pass = 0; pass < (TWO ? 2 : 1); ++pass) {
+      const __nv_bfloat16* g = pass == 0 ? g1 : g2;
+      const __nv_bfloat16* b = pass == 0 ? b1 : b2;
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += v[i][k];
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s / (float)D;
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+        if (sub + G * i < nvec)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float d = v[i][k] - mean;
+            q += d * d;
+          }
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+      const float rstd = 1.0f / sqrtf(q / (float)D + eps);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int c = sub + G * i;
+        if (c < nvec) {
+          float gf[8], bf[8];
+          unpack8(reinterpret_cast<const uint4*>(g)[c], gf);
+          if (b != nullptr) {
+            unpack8(reinterpret_cast<const uint4*>(b)[c], bf);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) bf[k] = 0.f;
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            v[i][k] = (v[i][k] - mean) * rstd;
+            v[i][k] = v[i][k] * gf[k] + bf[k];
+            if (TWO && pass == 0) v[i][k] = rbf(v[i][k]);
+          }
+        }
+      }
+    }
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int c = sub + G * i;
+        if (c < nvec) reinterpret_cast<uint4*>(y + r * ldy)[c] = pack8(v[i]);
+      }
+    }
+  }
+}
+
+template <int MAXV, int G>
+int launch_ln_fast(const void* x, int64_t M, int D, int64_t ldx, const void* g1, const void* b1,
+                   const void* g2, const void* b2, float eps, int two, void* y, int64_t ldy,
+                   cudaStream_t st) {
+  constexpr int rows_per_block = 8 * (32 / G);
+  int64_t blocks = (M + rows_per_block - 1) / rows_per_block;
+  const int64_t cap = 16 * (int64_t)num_sms();
+  if (blocks > cap) blocks = cap;
+  using B = __nv_bfloat16;
+  auto X = reinterpret_cast<const B*>(x);
+  auto Y = reinterpret_cast<B*>(y);
+  if (two)
+    return launch_pdl(layer_norm_bf16_kernel<MAXV, G, true>, dim3((unsigned)blocks), dim3(256), 0,
+                      st, X, M, D, ldx, reinterpret_cast<const B*>(g1),
+                      reinterpret_cast<const B*>(b1), reinterpret_cast<const B*>(g2),
+                      reinterpret_cast<const B*>(b2), eps, Y, ldy);
+  return launch_pdl(layer_norm_bf16_kernel<MAXV, G, false>, dim3((unsigned)blocks), dim3(256), 0,
+                    st, X, M, D, ldx, reinterpret_cast<const B*>(g1),
+                    reinterpret_cast<const B*>(b1), reinterpret_cast<const B*>(g2),
+                    reinterpret_cast<const B*>(b2), eps, Y, ldy);
+}
+
 template <typename T, int VEC, int MAXV>
 int launch_norm(const void* x, int64_t M, int D, int64_t ldx, const void* g1, const void* b1,
                 const void* g2, const void* b2, float eps, int mode, int two, void* y,
@@ -158,11 +267,10 @@ int launch_norm(const void* x, int64_t M, int D, int64_t ldx, const void* g1, co
   int64_t blocks = (M * 32 + 255) / 256;
   const int cap = 32 * num_sms();
   if (blocks > cap) blocks = cap;
-  row_norm_kernel<T, VEC, MAXV><<<(unsigned)blocks, 256, 0, st>>>(
+  return launch_pdl(row_norm_kernel<T, VEC, MAXV>, dim3((unsigned)blocks), dim3(256), 0, st,
       reinterpret_cast<const T*>(x), M, D, ldx, reinterpret_cast<const T*>(g1),
       reinterpret_cast<const T*>(b1), reinterpret_cast<const T*>(g2),
       reinterpret_cast<const T*>(b2), eps, mode, two, reinterpret_cast<T*>(y), ldy);
-  return check_launch();
 }
 
 template <typename T>
@@ -173,6 +281,16 @@ int dispatch_norm(const void* x, int64_t M, int D, int64_t ldx, const void* g1, 
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const bool vec = (D % V == 0) && ((ldx * (int64_t)sizeof(T)) % 16 == 0) &&
                    ((ldy * (int64_t)sizeof(T)) % 16 == 0) && al16(x) && al16(y);
+  if constexpr (sizeof(T) == 2) {
+    const bool params16 = al16(g1) && (b1 == nullptr || al16(b1)) &&
+                          (!two || (al16(g2) && (b2 == nullptr || al16(b2))));
+    if (vec && params16 && mode == CK_NORM_LAYER) {
+      const int nvec = D / 8;
+      if (nvec <= 32) return launch_ln_fast<4, 8>(x, M, D, ldx, g1, b1, g2, b2, eps, two, y, ldy, st);
+      if (nvec <= 64) return launch_ln_fast<4, 16>(x, M, D, ldx, g1, b1, g2, b2, eps, two, y, ldy, st);
+      if (nvec <= 128) return launch_ln_fast<4, 32>(x, M, D, ldx, g1, b1, g2, b2, eps, two, y, ldy, st);
+    }
+  }
   if (vec) {
     const int per = (D / V + 31) / 32;
     if (per <= 1) return launch_norm<T, V, 1>(x, M, D, ldx, g1, b1, g2, b2, eps, mode, two, y, ldy, st);

@@ -59,6 +59,8 @@ PackWs carve(void* ws, int64_t E, int32_t B) {
 
 __global__ void pack_count_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
                                   int32_t* counts, int32_t* flag) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e - lane < E;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -81,6 +83,8 @@ __global__ void pack_count_kernel(const void* bidx, int dt, int64_t stride, int6
 
 __global__ void pack_scan_kernel(const int32_t* counts, int32_t B, int32_t* offsets,
                                  int32_t* e_max) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t warp_max[32];
   const int t = threadIdx.x;
@@ -132,6 +136,8 @@ __global__ void pack_scan_kernel(const int32_t* counts, int32_t B, int32_t* offs
 
 __global__ void pack_rank_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
                                  PackWs w) {
+  grid_dep_wait();
+  grid_dep_launch();
   if (w.flag[0] == 0) return;  // sorted: ranks are not needed
   if (!w.has_matrix) {
     if (blockIdx.x == 0 && threadIdx.x == 0) set_status(CK_ERR_UNSUPPORTED, 1, 0);
@@ -161,6 +167,8 @@ __global__ void pack_rank_kernel(const void* bidx, int dt, int64_t stride, int64
 }
 
 __global__ void pack_colscan_kernel(PackWs w) {
+  grid_dep_wait();
+  grid_dep_launch();
   if (w.flag[0] == 0 || !w.has_matrix) return;
   __shared__ int32_t carry_s;
   __shared__ int32_t wt[8];
@@ -195,6 +203,8 @@ __global__ void pack_colscan_kernel(PackWs w) {
 
 __global__ void pack_dest_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
                                  const int32_t* offsets, PackWs w, int32_t* dest) {
+  grid_dep_wait();
+  grid_dep_launch();
   const bool unsorted = w.flag[0] != 0;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -218,6 +228,8 @@ __global__ void pack_scatter_kernel(const uint8_t* flat, int64_t row_bytes, int6
                                     const void* bidx, int dt, int64_t stride, int64_t E,
                                     const int32_t* dest, const int32_t* offsets, int32_t e_max,
                                     uint8_t* out, uint8_t* mask) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -261,20 +273,15 @@ int pack_events(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B, 
   if (E > 0) {
     int64_t blocks = (E + 255) / 256;
     if (blocks > 8 * sms) blocks = 8 * sms;
-    pack_count_kernel<<<(unsigned)blocks, 256, 0, st>>>(bidx, dt, stride, E, B, counts, w.flag);
-    if (check_launch()) return CK_ERR_CUDA;
+    if (launch_pdl(pack_count_kernel, dim3((unsigned)blocks), dim3(256), 0, st, bidx, dt, stride, E, B, counts, w.flag)) return CK_ERR_CUDA;
   }
-  pack_scan_kernel<<<1, 1024, 0, st>>>(counts, B, offsets, e_max);
-  if (check_launch()) return CK_ERR_CUDA;
+  if (launch_pdl(pack_scan_kernel, dim3(1), dim3(1024), 0, st, counts, B, offsets, e_max)) return CK_ERR_CUDA;
   if (E > 0) {
-    pack_rank_kernel<<<(unsigned)w.nchunks, CHUNK, 0, st>>>(bidx, dt, stride, E, B, w);
-    if (check_launch()) return CK_ERR_CUDA;
-    pack_colscan_kernel<<<(unsigned)B, 256, 0, st>>>(w);
-    if (check_launch()) return CK_ERR_CUDA;
+    if (launch_pdl(pack_rank_kernel, dim3((unsigned)w.nchunks), dim3(CHUNK), 0, st, bidx, dt, stride, E, B, w)) return CK_ERR_CUDA;
+    if (launch_pdl(pack_colscan_kernel, dim3((unsigned)B), dim3(256), 0, st, w)) return CK_ERR_CUDA;
     int64_t blocks = (E + 255) / 256;
     if (blocks > 8 * sms) blocks = 8 * sms;
-    pack_dest_kernel<<<(unsigned)blocks, 256, 0, st>>>(bidx, dt, stride, E, B, offsets, w, dest);
-    if (check_launch()) return CK_ERR_CUDA;
+    if (launch_pdl(pack_dest_kernel, dim3((unsigned)blocks), dim3(256), 0, st, bidx, dt, stride, E, B, offsets, w, dest)) return CK_ERR_CUDA;
   }
   return CK_OK;
 }
@@ -295,18 +302,16 @@ int pack_scatter(const void* flat, int dtype, int64_t E, int32_t D, int64_t flat
   const bool v16 = (row_bytes % 16 == 0) && (fs_b % 16 == 0) &&
                    ((reinterpret_cast<uintptr_t>(flat) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   if (v16)
-    pack_scatter_kernel<uint4><<<(unsigned)blocks, 256, 0, st>>>(
+    return launch_pdl(pack_scatter_kernel<uint4>, dim3((unsigned)blocks), dim3(256), 0, st,
         reinterpret_cast<const uint8_t*>(flat), row_bytes, fs_b, bidx, dt, stride, E, dest,
         offsets, e_max, reinterpret_cast<uint8_t*>(out), mask);
-  else if (es == 4)
-    pack_scatter_kernel<uint32_t><<<(unsigned)blocks, 256, 0, st>>>(
+  if (es == 4)
+    return launch_pdl(pack_scatter_kernel<uint32_t>, dim3((unsigned)blocks), dim3(256), 0, st,
         reinterpret_cast<const uint8_t*>(flat), row_bytes, fs_b, bidx, dt, stride, E, dest,
         offsets, e_max, reinterpret_cast<uint8_t*>(out), mask);
-  else
-    pack_scatter_kernel<uint16_t><<<(unsigned)blocks, 256, 0, st>>>(
-        reinterpret_cast<const uint8_t*>(flat), row_bytes, fs_b, bidx, dt, stride, E, dest,
-        offsets, e_max, reinterpret_cast<uint8_t*>(out), mask);
-  return check_launch();
+  return launch_pdl(pack_scatter_kernel<uint16_t>, dim3((unsigned)blocks), dim3(256), 0, st,
+      reinterpret_cast<const uint8_t*>(flat), row_bytes, fs_b, bidx, dt, stride, E, dest,
+      offsets, e_max, reinterpret_cast<uint8_t*>(out), mask);
 }
 
 }  // namespace ck

@@ -2,6 +2,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_set>
 
@@ -38,14 +40,38 @@ int record_cuda_error() {
   return CK_ERR_CUDA;
 }
 
-int check_launch() {
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+namespace {
+int check_launch_noc() {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     t_last_cuda_error = (int)e;
     return CK_ERR_CUDA;
   }
   return CK_OK;
+}
+}  // namespace
+
+int check_launch() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return check_launch_noc();
+}
+
+int finish_launch(cudaError_t e) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    t_last_cuda_error = (int)e;
+    return CK_ERR_CUDA;
+  }
+  return check_launch_noc();
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("CK_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
 }
 
 bool smem_attr_ready(const void* kernel, int bytes) {

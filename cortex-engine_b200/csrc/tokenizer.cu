@@ -4,9 +4,9 @@
 //   out[dest[e], :] = n_emb[nid[e], :] + t_emb[tb[e], :] + v_emb[val[e], :]
 //
 // evaluated left to right in the table dtype, so bf16 tables give
-// bf16(bf16(n + t) + v) exactly as torch eager does. One warp per event; each
-// lane moves 16-byte vectors of the three rows (D = 512 bf16: 2 vectors per
-// lane per table). With gamma != NULL the finished row is LayerNorm-ed in
+// bf16(bf16(n + t) + v) exactly as torch eager does. A group of lanes per
+// event (16 for D = 512 bf16, two events per warp); each lane moves 16-byte
+// vectors of the three rows (4 vectors per lane per table at D = 512). With gamma != NULL the finished row is LayerNorm-ed in
 // registers before the store, which fuses CrossAttentionBlock.norm_kv
 // (cortex/models/perceiver.py:68) into the gather: the raw tokens never reach HBM.
 // Out-of-range indices set CK_ERR_INDEX and write a zero row.
@@ -65,11 +65,18 @@ struct TokArgs {
   int D;
 };
 
-// VEC: elements per vector access (Vec<T>::N, or 1 for unaligned shapes).
-// MAXV: vectors per lane kept in registers (LayerNorm needs the whole row).
-template <typename T, int VEC, int MAXV, bool LN>
-__global__ void tokenize_kernel(const TokArgs a) {
+// G lanes share one event row (G in {8, 16, 32}, so a warp handles 32 / G
+// events at once); each lane holds MAXV vectors of VEC elements. Index loads,
+// the three table gathers and the output store of the 32 / G rows are all
+// independent, so a warp keeps 3 * MAXV * (32 / G) 16-byte loads in flight.
+template <typename T, int VEC, int MAXV, bool LN, int G>
+__global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const TokArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  constexpr int RPW = 32 / G;
   const int lane = threadIdx.x & 31;
+  const int sub = lane % G;
+  const int slot = lane / G;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const T* ne = reinterpret_cast<const T*>(a.n_emb);
@@ -77,114 +84,139 @@ __global__ void tokenize_kernel(const TokArgs a) {
   const T* ve = reinterpret_cast<const T*>(a.v_emb);
   T* out = reinterpret_cast<T*>(a.out);
   const int nvec = a.D / VEC;
-  for (int64_t e = warp; e < a.E; e += nwarps) {
-    const int64_t dst_row = a.dest ? (int64_t)a.dest[e] : e;
-    if (dst_row < 0) continue;
-    const int64_t n = load_idx(a.nid, a.idx_dt, e, a.s_nid);
-    const int64_t t = load_idx(a.tb, a.idx_dt, e, a.s_tb);
-    const int64_t v = load_idx(a.val, a.idx_dt, e, a.s_val);
-    const bool ok = n >= 0 && n < a.n_vocab && t >= 0 && t < a.t_vocab && v >= 0 && v < a.v_vocab;
-    if (!ok && lane == 0) set_status(CK_ERR_INDEX, (int)e, (int)(n < 0 || n >= a.n_vocab ? n : (t < 0 || t >= a.t_vocab ? t : v)));
+  for (int64_t base = warp * RPW; base < a.E; base += nwarps * RPW) {
+    const int64_t e = base + slot;
+    const bool live = e < a.E;
+    int64_t dst_row = -1, n = 0, t = 0, v = 0;
+    if (live) {
+      dst_row = a.dest ? (int64_t)a.dest[e] : e;
+      n = load_idx(a.nid, a.idx_dt, e, a.s_nid);
+      t = load_idx(a.tb, a.idx_dt, e, a.s_tb);
+      v = load_idx(a.val, a.idx_dt, e, a.s_val);
+    }
+    const bool in_range =
+        n >= 0 && n < a.n_vocab && t >= 0 && t < a.t_vocab && v >= 0 && v < a.v_vocab;
+    const bool store = live && dst_row >= 0;
+    const bool ok = store && in_range;
+    if (store && !in_range && sub == 0)
+      set_status(CK_ERR_INDEX, (int)e,
+                 (int)(n < 0 || n >= a.n_vocab ? n : (t < 0 || t >= a.t_vocab ? t : v)));
     float x[MAXV][VEC];
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        if (ok) {
-          float fn[VEC], ft[VEC], fv[VEC];
-          if constexpr (VEC == 1) {
-            fn[0] = (float)ne[n * a.n_ld + c];
-            ft[0] = (float)te[t * a.t_ld + c];
-            fv[0] = (float)ve[v * a.v_ld + c];
-          } else {
-            Vec<T>::load(ne + n * a.n_ld + c * VEC, fn);
-            Vec<T>::load(te + t * a.t_ld + c * VEC, ft);
-            Vec<T>::load(ve + v * a.v_ld + c * VEC, fv);
-          }
+      const int c = sub + G * i;
 #pragma unroll
-          for (int k = 0; k < VEC; ++k)
-            x[i][k] = Vec<T>::round(Vec<T>::round(fn[k] + ft[k]) + fv[k]);
+      for (int k = 0; k < VEC; ++k) x[i][k] = 0.f;
+      if (ok && c < nvec) {
+        float fn[VEC], ft[VEC], fv[VEC];
+        if constexpr (VEC == 1) {
+          fn[0] = (float)ne[n * a.n_ld + c];
+          ft[0] = (float)te[t * a.t_ld + c];
+          fv[0] = (float)ve[v * a.v_ld + c];
         } else {
-#pragma unroll
-          for (int k = 0; k < VEC; ++k) x[i][k] = 0.f;
+          Vec<T>::load(ne + n * a.n_ld + c * VEC, fn);
+          Vec<T>::load(te + t * a.t_ld + c * VEC, ft);
+          Vec<T>::load(ve + v * a.v_ld + c * VEC, fv);
         }
+#pragma unroll
+        for (int k = 0; k < VEC; ++k)
+          x[i][k] = Vec<T>::round(Vec<T>::round(fn[k] + ft[k]) + fv[k]);
       }
     }
-    if (LN && ok) {
+    if (LN) {
+      // Two-pass mean / biased variance over the G lanes of the row (all 32
+      // lanes take part in the shuffles; rows that are not stored discard it).
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < MAXV; ++i)
-        if (lane + 32 * i < nvec)
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) s += x[i][k];
-      const float mean = warp_sum(s) / (float)a.D;
+        for (int k = 0; k < VEC; ++k) s += x[i][k];
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s / (float)a.D;
       float q = 0.f;
 #pragma unroll
       for (int i = 0; i < MAXV; ++i)
-        if (lane + 32 * i < nvec)
+        if (sub + G * i < nvec)
 #pragma unroll
           for (int k = 0; k < VEC; ++k) {
             const float d = x[i][k] - mean;
             q += d * d;
           }
-      const float var = warp_sum(q) / (float)a.D;
-      const float rstd = 1.0f / sqrtf(var + a.eps);
-      const T* g = reinterpret_cast<const T*>(a.gamma);
-      const T* bt = reinterpret_cast<const T*>(a.beta);
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nvec) {
+      for (int o = G / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+      const float rstd = 1.0f / sqrtf(q / (float)a.D + a.eps);
+      if (ok) {
+        const T* g = reinterpret_cast<const T*>(a.gamma);
+        const T* bt = reinterpret_cast<const T*>(a.beta);
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) {
-            const float gk = (float)g[c * VEC + k];
-            const float bk = bt ? (float)bt[c * VEC + k] : 0.f;
-            x[i][k] = (x[i][k] - mean) * rstd * gk + bk;
+        for (int i = 0; i < MAXV; ++i) {
+          const int c = sub + G * i;
+          if (c < nvec) {
+            float gk[VEC], bk[VEC];
+            if constexpr (VEC == 1) {
+              gk[0] = (float)g[c];
+              bk[0] = bt ? (float)bt[c] : 0.f;
+            } else {
+              Vec<T>::load(g + c * VEC, gk);
+              if (bt) {
+                Vec<T>::load(bt + c * VEC, bk);
+              } else {
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) bk[k] = 0.f;
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) x[i][k] = (x[i][k] - mean) * rstd * gk[k] + bk[k];
           }
         }
       }
     }
+    if (store) {
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        if constexpr (VEC == 1) {
-          out[dst_row * a.out_ld + c] = (T)x[i][0];
-        } else {
-          Vec<T>::store(out + dst_row * a.out_ld + c * VEC, x[i]);
+      for (int i = 0; i < MAXV; ++i) {
+        const int c = sub + G * i;
+        if (c < nvec) {
+          if constexpr (VEC == 1) {
+            out[dst_row * a.out_ld + c] = (T)x[i][0];
+          } else {
+            Vec<T>::store(out + dst_row * a.out_ld + c * VEC, x[i]);
+          }
         }
       }
     }
   }
 }
 
-template <typename T, int VEC, int MAXV, bool LN>
+template <typename T, int VEC, int MAXV, bool LN, int G>
 int launch_tok(const TokArgs& a, cudaStream_t st) {
-  int64_t blocks = (a.E * 32 + 255) / 256;
-  const int cap = 32 * num_sms();
+  constexpr int rows_per_block = 8 * (32 / G);
+  int64_t blocks = (a.E + rows_per_block - 1) / rows_per_block;
+  const int64_t cap = 16 * (int64_t)num_sms();
   if (blocks > cap) blocks = cap;
-  tokenize_kernel<T, VEC, MAXV, LN><<<(unsigned)blocks, 256, 0, st>>>(a);
-  return check_launch();
+  return launch_pdl(tokenize_kernel<T, VEC, MAXV, LN, G>, dim3((unsigned)blocks), dim3(256), 0,
+                    st, a);
+}
+
+template <typename T, int VEC, int MAXV, int G>
+int launch_tok_ln(const TokArgs& a, cudaStream_t st) {
+  return a.gamma != nullptr ? launch_tok<T, VEC, MAXV, true, G>(a, st)
+                            : launch_tok<T, VEC, MAXV, false, G>(a, st);
 }
 
 template <typename T>
 int dispatch_tok(const TokArgs& a, bool vec_ok, cudaStream_t st) {
   constexpr int V = Vec<T>::N;
-  const bool ln = a.gamma != nullptr;
   if (vec_ok) {
-    const int per_lane = (a.D / V + 31) / 32;
-    if (per_lane <= 2) return ln ? launch_tok<T, V, 2, true>(a, st) : launch_tok<T, V, 2, false>(a, st);
-    if (per_lane <= 4) return ln ? launch_tok<T, V, 4, true>(a, st) : launch_tok<T, V, 4, false>(a, st);
-    if (per_lane <= 8) return ln ? launch_tok<T, V, 8, true>(a, st) : launch_tok<T, V, 8, false>(a, st);
-    if (!ln) {
-      // long rows without a norm: process in register-sized column slices
-      return CK_ERR_UNSUPPORTED;
-    }
+    const int nvec = a.D / V;
+    if (nvec <= 32) return launch_tok_ln<T, V, 4, 8>(a, st);
+    if (nvec <= 64) return launch_tok_ln<T, V, 4, 16>(a, st);
+    if (nvec <= 128) return launch_tok_ln<T, V, 4, 32>(a, st);
+    if (nvec <= 256) return launch_tok_ln<T, V, 8, 32>(a, st);
     return CK_ERR_UNSUPPORTED;
   }
-  const int per_lane = (a.D + 31) / 32;
-  if (per_lane <= 8) return ln ? launch_tok<T, 1, 8, true>(a, st) : launch_tok<T, 1, 8, false>(a, st);
-  if (per_lane <= 32) return ln ? launch_tok<T, 1, 32, true>(a, st) : launch_tok<T, 1, 32, false>(a, st);
+  if (a.D <= 256) return launch_tok_ln<T, 1, 8, 32>(a, st);
+  if (a.D <= 1024) return launch_tok_ln<T, 1, 32, 32>(a, st);
   return CK_ERR_UNSUPPORTED;
 }
 
@@ -206,7 +238,8 @@ int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const bool vec_ok = ((int64_t)D * es) % 16 == 0 && (n_ld * es) % 16 == 0 &&
                       (t_ld * es) % 16 == 0 && (v_ld * es) % 16 == 0 && (out_ld * es) % 16 == 0 &&
-                      al16(n_emb) && al16(t_emb) && al16(v_emb) && al16(out);
+                      al16(n_emb) && al16(t_emb) && al16(v_emb) && al16(out) &&
+                      (gamma == nullptr || al16(gamma)) && (beta == nullptr || al16(beta));
   if (dtype == CK_BF16) return dispatch_tok<__nv_bfloat16>(a, vec_ok, st);
   if (dtype == CK_F32) return dispatch_tok<float>(a, vec_ok, st);
   return CK_ERR_UNSUPPORTED;

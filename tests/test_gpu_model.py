@@ -149,3 +149,88 @@ def test_empty_window_inside_batch():
     ref = O.forward(p, wl.config, nid, tb, val, bidx)
     assert y.shape == (3, 2) and torch.isfinite(y).all()
     assert _rel(y, ref) <= TOL["bfloat16"]
+
+
+@pytest.mark.parametrize("name,latents,layers", [("cfg1", None, 1), ("cfg4", None, 1),
+                                                  ("cfg1", 200, 1), ("cfg1", 64, 1),
+                                                  ("cfg1", 1000, 1)])
+def test_fused_head_matches_composed_head(monkeypatch, name, latents, layers):
+    """The behaviour head in algebraic form (one clustered tcgen05 kernel on the
+    weight-only matrix W_k^T q / W_v^T w_out) against the composed head (both
+    LayerNorms, head kv_proj, 2-query attention, out_proj D->1) and the oracle.
+    Covers partial 128-latent tiles (L=200, L=64), an 8-CTA cluster (L=1000)
+    and the D768/H12 geometry (cfg4: 24 score pairs, 3 vectors per lane)."""
+    import dataclasses
+
+    from cortex.workloads import WORKLOADS, build_model, make_inputs
+
+    wl = WORKLOADS[name]
+    upd = {"num_layers": layers}
+    if latents is not None:
+        upd["num_latents"] = latents
+    wl = dataclasses.replace(wl, config=wl.config.model_copy(update=upd))
+    model = build_model(wl, DEV)
+    inp, _ = make_inputs(wl, seed=4, batch=6)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        monkeypatch.setenv("CK_HEAD_FUSED", "1")
+        fused = model(*(inp[k] for k in cols))["behavior"]
+        monkeypatch.setenv("CK_HEAD_FUSED", "0")
+        composed = model(*(inp[k] for k in cols))["behavior"]
+    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
+           for k, v in model.state_dict().items()}
+    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
+    assert torch.isfinite(fused).all()
+    assert _rel(fused, composed) <= 1e-2, _rel(fused, composed)
+    assert _rel(fused, ref) <= TOL["bfloat16"], _rel(fused, ref)
+    assert _rel(fused, ref) <= max(1.5 * _rel(composed, ref), 5e-3)
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
+def test_norm_fold_matches_separate_norms(monkeypatch, name):
+    """LayerNorms folded into qkv_proj / mlp.0 (raw residual into the GEMM,
+    statistics from the producing residual epilogue) against separate norm
+    kernels and the oracle. cfg2 keeps its INT8 qkv / mlp.0 unfolded while the
+    INT8 residual GEMMs still run; cfg3 is ragged."""
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    with torch.no_grad():  # non-trivial affine parameters, so the fold is exercised
+        g = torch.Generator(device="cpu").manual_seed(5)
+        for blk in model.encoder.self_attn_blocks:
+            for nrm in (blk.norm_attn, blk.norm_mlp):
+                nrm.weight.copy_(1 + 0.2 * torch.randn(nrm.weight.shape, generator=g))
+                nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
+    inp, _ = make_inputs(wl, seed=6, batch=8)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        monkeypatch.setenv("CK_NORM_FOLD", "1")
+        folded = model(*(inp[k] for k in cols))["behavior"]
+        monkeypatch.setenv("CK_NORM_FOLD", "0")
+        separate = model(*(inp[k] for k in cols))["behavior"]
+    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
+           for k, v in model.state_dict().items()}
+    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
+    assert torch.isfinite(folded).all()
+    assert _rel(folded, separate) <= 1e-2, _rel(folded, separate)
+    assert _rel(folded, ref) <= TOL["bfloat16"], _rel(folded, ref)
+
+
+def test_norm_fold_follows_inplace_parameter_updates():
+    """The folded weights are derived data: an in-place update of a norm or a
+    linear weight (version counter) rebuilds them before the next forward."""
+    from cortex.workloads import make_inputs
+
+    wl, model = _model("cfg1")
+    inp, _ = make_inputs(wl, seed=7, batch=4)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        before = model(*(inp[k] for k in cols))["behavior"]
+        model.encoder.self_attn_blocks[0].norm_attn.weight.mul_(1.7)
+        model.encoder.self_attn_blocks[2].mlp[0].weight.mul_(0.5)
+        after = model(*(inp[k] for k in cols))["behavior"]
+    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
+           for k, v in model.state_dict().items()}
+    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
+    assert not torch.equal(before, after)
+    assert _rel(after, ref) <= TOL["bfloat16"], _rel(after, ref)

@@ -50,7 +50,8 @@ def test_ctypes_structs_match_header_layout(tmp_path):
     if shutil.which("gcc") is None:
         pytest.skip("gcc not available")
     structs = {"ck_attention_args": _lib.AttentionArgs, "ck_linear_weight": _lib.LinearWeight,
-               "ck_block_weights": _lib.BlockWeights, "ck_model": _lib.Model}
+               "ck_norm_fold": _lib.NormFold, "ck_block_weights": _lib.BlockWeights,
+               "ck_model": _lib.Model}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "cortex_b200.h"',
              'int main(void) {']
     for cname, py in structs.items():
