@@ -16,6 +16,7 @@ copied to the model's device, asynchronously when pinned) or on the device.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from typing import cast
 
@@ -204,6 +205,8 @@ class CortexModel(nn.Module):
 
     def _fold(self, norm: nn.Module, lin: nn.Module, keep: list, folds: list) -> L.NormFold:
         nf = L.NormFold()
+        if os.environ.get("CK_NORM_FOLD") != "1":  # folding is opt-in (see ck_forward)
+            return nf
         w = getattr(lin, "weight", None)
         if (w is None or w.dtype != torch.bfloat16 or getattr(lin, "bias", None) is not None
                 or w.dim() != 2 or w.shape[1] % 8 != 0 or not w.is_contiguous()

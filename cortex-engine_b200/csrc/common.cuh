@@ -140,37 +140,63 @@ __device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsign
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+__device__ __forceinline__ unsigned long long fadd2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsigned long long b) {
   unsigned long long d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 
-// gelu_as on two values with the polynomial and the squarings in paired fp32
-// instructions (same arithmetic, same rounding as gelu_as per element).
-__device__ __forceinline__ void gelu_as2(float& a, float& b) {
-  const float ya = fminf(fabsf(a) * 0.70710678118654752440f, 1.0e4f);
-  const float yb = fminf(fabsf(b) * 0.70710678118654752440f, 1.0e4f);
-  const unsigned long long y = f2pk(ya, yb);
-  unsigned long long q = ffma2(f2pk(4.30638e-5f, 4.30638e-5f), y,
-                               f2pk(2.765672e-4f, 2.765672e-4f));
-  q = ffma2(q, y, f2pk(1.520143e-4f, 1.520143e-4f));
-  q = ffma2(q, y, f2pk(9.2705272e-3f, 9.2705272e-3f));
-  q = ffma2(q, y, f2pk(4.22820123e-2f, 4.22820123e-2f));
-  q = ffma2(q, y, f2pk(7.05230784e-2f, 7.05230784e-2f));
-  q = ffma2(q, y, f2pk(1.0f, 1.0f));
+// bf16 pair conversions: one cvt for two values (round to nearest even).
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float bf16_lo(uint32_t r) { return __uint_as_float(r << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t r) { return __uint_as_float(r & 0xffff0000u); }
+// Round two fp32 values through bf16 (torch's bf16 op output), one conversion.
+__device__ __forceinline__ void rbf2(float& a, float& b) {
+  const uint32_t r = cvt_bf16x2(a, b);
+  a = bf16_lo(r);
+  b = bf16_hi(r);
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU of a pair, x >= kGeluTail: the same A&S 7.1.28 evaluation as gelu_as,
+// arranged for fewer instructions. The polynomial runs on |x| with its
+// coefficients pre-scaled by 2^(-k/2) (erf's argument is x / sqrt 2) and by
+// 2^(1/16), so the 16th power of the reciprocal is t = (1 - erf(|x|/sqrt 2)) / 2
+// = Phi(-|x|) directly; then GELU(x) = x * (x >= 0 ? 1 - t : t).
+__device__ __forceinline__ void gelu_pair(float& a, float& b) {
+  const unsigned long long y = f2pk(fabsf(a), fabsf(b));
+  unsigned long long q = ffma2(f2pk(5.6212996639622074e-06f, 5.6212996639622074e-06f), y,
+                               f2pk(5.1055209008659824e-05f, 5.1055209008659824e-05f));
+  q = ffma2(q, y, f2pk(3.96861370110139e-05f, 3.96861370110139e-05f));
+  q = ffma2(q, y, f2pk(3.422739238900824e-03f, 3.422739238900824e-03f));
+  q = ffma2(q, y, f2pk(2.2076998456581714e-02f, 2.2076998456581714e-02f));
+  q = ffma2(q, y, f2pk(5.207516303663057e-02f, 5.207516303663057e-02f));
+  q = ffma2(q, y, f2pk(1.0442737824274138f, 1.0442737824274138f));
   float qa, qb;
   f2up(q, qa, qb);
-  unsigned long long r = f2pk(__fdividef(1.0f, qa), __fdividef(1.0f, qb));
-  r = fmul2(r, r);
-  r = fmul2(r, r);
-  r = fmul2(r, r);
-  r = fmul2(r, r);
-  const unsigned long long h = fmul2(fmul2(f2pk(0.5f, 0.5f), f2pk(a, b)), r);
-  float ha, hb;
-  f2up(h, ha, hb);
-  a = a >= 0.f ? a - ha : ha;
-  b = b >= 0.f ? b - hb : hb;
+  unsigned long long t = f2pk(rcp_approx(qa), rcp_approx(qb));
+  t = fmul2(t, t);
+  t = fmul2(t, t);
+  t = fmul2(t, t);
+  t = fmul2(t, t);
+  float ta, tb;
+  f2up(t, ta, tb);
+  const unsigned long long phi = f2pk(a >= 0.f ? 1.f - ta : ta, b >= 0.f ? 1.f - tb : tb);
+  f2up(fmul2(f2pk(a, b), phi), a, b);
 }
 
 // Kept out of line so that the compiler cannot if-convert the rare tail path
@@ -181,10 +207,10 @@ static __device__ __noinline__ float gelu_tail(float x) { return gelu_erf(x); }
 // lane of the warp holds a tail value, which is rare after a LayerNorm -- the
 // library-erf form for the tail elements. All 32 lanes of the warp must call it.
 __device__ __forceinline__ void gelu32(float* v) {
-  bool tail = false;
+  float lo = v[0];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) tail |= (v[i] < kGeluTail);
-  if (__any_sync(0xffffffffu, tail)) {
+  for (int i = 1; i < 32; ++i) lo = fminf(lo, v[i]);
+  if (__any_sync(0xffffffffu, lo < kGeluTail)) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       if (v[i] < kGeluTail)
@@ -194,7 +220,7 @@ __device__ __forceinline__ void gelu32(float* v) {
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
+    for (int i = 0; i < 32; i += 2) gelu_pair(v[i], v[i + 1]);
   }
 }
 

@@ -34,6 +34,10 @@ struct GemmArgs {
 
 enum Fuse { FUSE_NONE = 0, FUSE_NORM = 1, FUSE_STATS = 2 };
 
+__device__ __forceinline__ int64_t residual_row(const GemmArgs& p, int m) {
+  return p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;
+}
+
 // Producer statistics of one row (up to 8 segments), fetched ahead of use.
 struct StatsRow {
   float2 seg[8];
@@ -68,13 +72,18 @@ __device__ __forceinline__ void combine_stats(const GemmArgs& p, const StatsRow&
   rstd = 1.0f / sqrtf(m2 / (float)p.K + p.norm_eps);
 }
 
-// Epilogue math for 32 consecutive columns n0.. of row m (v: fp32 accumulators).
+// Epilogue math for 32 consecutive columns n0.. of row m (v: fp32 accumulators),
+// result packed as 16 bf16 pairs in out.
 // FUSE_NORM applies the folded LayerNorm with the row's (mean, rstd) first.
 // fold: the (colsum, bias) pairs of columns n0..n0+31 in shared memory.
+// res: the residual row's 32 columns (RESID) when the caller prefetched them
+// (whole chunks), else NULL and the residual is read here.
+// The linear output is rounded to bf16 as F.linear returns it; for STORE that
+// rounding is the final pack itself.
 template <int EPI, int FUSE = FUSE_NONE>
 __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, float* v,
-                                              float mean = 0.f, float rstd = 0.f,
-                                              const float2* fold = nullptr) {
+                                              float mean, float rstd, const float2* fold,
+                                              const uint4* res, uint32_t* out) {
   const bool full = (n0 + 32 <= p.N);
   if (FUSE == FUSE_NORM) {
 #pragma unroll
@@ -99,26 +108,31 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, 
       for (int i = 0; i < 32; ++i) v[i] *= (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
     }
   }
+  if (EPI != CK_EPI_STORE) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = rbf(v[i]);  // linear output in bf16, as F.linear returns it
+    for (int i = 0; i < 32; i += 2) rbf2(v[i], v[i + 1]);
+  }
   if (EPI == CK_EPI_GELU) {
     gelu32(v);
-  } else if (EPI == CK_EPI_RESID || EPI == CK_EPI_BIAS) {
-    if (m >= p.M) return;
+  } else if ((EPI == CK_EPI_RESID || EPI == CK_EPI_BIAS) && m < p.M) {
     const __nv_bfloat16* src;
     if (EPI == CK_EPI_RESID) {
-      const int64_t r = p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;
-      src = p.aux + r * p.ld_aux + n0;
+      src = p.aux + residual_row(p, m) * p.ld_aux + n0;
     } else {
       src = p.aux + n0;
     }
     if (full) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float f[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(src) + c), f);
+        const uint4 u = res != nullptr ? res[c] : __ldg(reinterpret_cast<const uint4*>(src) + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[8 * c + j] = f[j] + v[8 * c + j];
+        for (int j = 0; j < 4; ++j) {
+          float lo = v[8 * c + 2 * j], hi = v[8 * c + 2 * j + 1];
+          f2up(fadd2(f2pk(bf16_lo(w[j]), bf16_hi(w[j])), f2pk(lo, hi)), lo, hi);
+          v[8 * c + 2 * j] = lo;
+          v[8 * c + 2 * j + 1] = hi;
+        }
       }
     } else {
 #pragma unroll
@@ -126,6 +140,8 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, 
         if (n0 + i < p.N) v[i] = bf2f(src[i]) + v[i];
     }
   }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out[i] = cvt_bf16x2(v[2 * i], v[2 * i + 1]);
 }
 
 }  // namespace gemm

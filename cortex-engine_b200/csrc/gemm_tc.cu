@@ -12,9 +12,12 @@
 //   warp 0       TMA producer: A and B tiles into a STAGES-deep smem ring
 //   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2..9   epilogue: two warps per TMEM lane quarter, each taking half of
-//                the tile's columns: tcgen05.ld of the fp32 accumulator, the
-//                epilogue op (scale, bf16 rounding, GELU / residual / bias),
-//                staging in 64B-swizzled smem and a TMA tile store
+//                the tile's columns in 32-column chunks: tcgen05.ld of the fp32
+//                accumulator (the next chunk's read and residual load in flight
+//                while the current one is finished), the epilogue op (folded
+//                norm, scale, bf16 rounding, GELU / residual / bias, row
+//                statistics), a 64B-swizzled 32 x 32 smem box per chunk (two
+//                per warp, alternating) and one TMA tile store per chunk
 //   warps 10..13 (int8 only) int8 -> bf16 converter
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1. All mbarrier waits are bounded
@@ -36,7 +39,7 @@ using gemm::epilogue_math;
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int EPI_WARPS = 8;
-constexpr int STG_BOX = 32 * 64 * 2;  // one 32-row x 64-col bf16 store box (128B rows)
+constexpr int STG_BOX = 32 * 32 * 2;  // one 32-row x 32-col bf16 store box (64B rows)
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
@@ -46,8 +49,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
   static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
-  // per epilogue warp: one 32x64 store box, reused by its rounds of 64 columns
-  static constexpr int STG_WARP = STG_BOX;
+  // per epilogue warp: two 32-row x 32-column bf16 store boxes (64B-swizzled)
+  static constexpr int STG_WARP = 2 * STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
   static constexpr int BAR_BYTES = 256;
   // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
@@ -76,7 +79,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
   uint8_t* sB8 = sB + C::STAGES * C::B_BYTES;
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
   float2* sFold = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);  // [8][2][BN/2] (FUSE_NORM)
-  uint8_t* sBar = sStg + C::EPI_SMEM + C::FOLD_SMEM;
+  uint8_t* sBar = reinterpret_cast<uint8_t*>(sFold) + C::FOLD_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
   uint64_t* conv = empty + C::STAGES;
@@ -207,8 +210,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int half = e >> 2;
     const int row = quarter * 32 + lane;
+    constexpr int NCH = BN / 64;  // 32-column chunks per warp per tile
     uint8_t* stg = sStg + e * C::STG_WARP;
-    constexpr int NCH = BN / 64;  // 32-column chunks per warp
     int acc = 0;
     uint32_t acc_phase = 0;
     // Folded LayerNorm (FUSE_NORM): the next tile's row statistics and column
@@ -252,39 +255,66 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
       const int m = mt * BM + row;
       float st_shift = 0.f, st_s1 = 0.f, st_s2 = 0.f;  // segment statistics (FUSE_STATS)
       int st_cnt = 0;
-      const int m0 = mt * BM + quarter * 32;
       const int col0 = half * (BN / 2);
-      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      // rounds of 64 columns: one batched TMEM read each (TMEM handed back to the
-      // MMA warp after the last read), epilogue math, a 128B-swizzled 32x64 box
-      // in smem and one TMA store per round
-#pragma unroll 1
-      for (int r = 0; r < NCH / 2; ++r) {
-        float v[64];
-        tmem_ld32(tbase + (uint32_t)(col0 + r * 64), v);
-        tmem_ld32(tbase + (uint32_t)(col0 + r * 64 + 32), v + 32);
-        tc_wait_ld();
-        if (r == NCH / 2 - 1) {
+      const int nbase = nt * BN + col0;
+      const uint32_t tbase =
+          tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + col0);
+      const bool row_ok = m < p.M;
+      const int m0 = mt * BM + quarter * 32;
+      const __nv_bfloat16* rrow =
+          (EPI == CK_EPI_RESID && row_ok) ? p.aux + gemm::residual_row(p, m) * p.ld_aux : nullptr;
+      // 32-column chunks, TMEM reads double-buffered: chunk c + 1 (and its
+      // residual) is in flight while chunk c is finished and handed to a TMA
+      // store; TMEM goes back to the MMA warp as soon as the last chunk has
+      // been read.
+      float va[32], vb[32];
+      uint4 ra[4], rb[4];
+      // (the int8 variant, short of registers beside its converter warps, reads
+      // the residual inside the epilogue math instead)
+      constexpr bool kPrefetch = EPI == CK_EPI_RESID && WMODE != W_I8_NK;
+      auto fetch_res = [&](int c, uint4* dst) {
+        if (kPrefetch && row_ok && nbase + c * 32 + 32 <= p.N) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = __ldg(reinterpret_cast<const uint4*>(rrow + nbase + c * 32) + q);
+        }
+      };
+      tmem_ld32(tbase, va);
+      fetch_res(0, ra);
+      tc_wait_ld();
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float* cur = (c & 1) ? vb : va;
+        float* nxt = (c & 1) ? va : vb;
+        uint4* rcur = (c & 1) ? rb : ra;
+        uint4* rnxt = (c & 1) ? ra : rb;
+        if (c + 1 < NCH) {
+          tmem_ld32(tbase + (uint32_t)((c + 1) * 32), nxt);
+          fetch_res(c + 1, rnxt);
+        } else {
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
-        const int nb = nt * BN + col0 + r * 64;
+        const int n0 = nbase + c * 32;
+        if (n0 < p.N) {
+          uint32_t packed[16];
+          epilogue_math<EPI, FUSE>(p, m, n0, cur, nmean, nrstd, wfold + acc * (BN / 2) + c * 32,
+                                   (kPrefetch && n0 + 32 <= p.N) ? rcur : nullptr, packed);
+          if (FUSE == gemm::FUSE_STATS) {
+            // statistics of the values as stored (bf16), shifted by the
+            // segment's first value so the sum of squares does not cancel
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-          if (nb + c * 32 < p.N)
-            epilogue_math<EPI, FUSE>(p, m, nb + c * 32, v + 32 * c, nmean, nrstd,
-                                     wfold + acc * (BN / 2) + r * 64 + c * 32);
-        if (FUSE == gemm::FUSE_STATS && nb < p.N) {
-          // statistics of the values as stored (bf16), shifted by the segment's
-          // first value so the sum of squares does not cancel
-#pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = rbf(v[i]);
-          if (r == 0) st_shift = v[0];
-          if (nb + 64 <= p.N) {
+            for (int i = 0; i < 16; ++i) {
+              cur[2 * i] = bf16_lo(packed[i]);
+              cur[2 * i + 1] = bf16_hi(packed[i]);
+            }
+            if (c == 0) st_shift = cur[0];
             float s1a = 0.f, s1b = 0.f, s2a = 0.f, s2b = 0.f;
 #pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-              const float d0 = v[i] - st_shift, d1 = v[i + 1] - st_shift;
+            for (int i = 0; i < 32; i += 2) {
+              const bool ok0 = n0 + i < p.N, ok1 = n0 + i + 1 < p.N;
+              const float d0 = ok0 ? cur[i] - st_shift : 0.f;
+              const float d1 = ok1 ? cur[i + 1] - st_shift : 0.f;
               s1a += d0;
               s1b += d1;
               s2a = fmaf(d0, d0, s2a);
@@ -292,31 +322,25 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
             }
             st_s1 += s1a + s1b;
             st_s2 += s2a + s2b;
-            st_cnt += 64;
-          } else {
+            st_cnt += min(32, p.N - n0);
+          }
+          // 64B-swizzled 32 x 32 box, then one TMA store per chunk; the box was
+          // last read by the store issued two chunks ago
+          uint8_t* box = stg + (c & 1) * STG_BOX;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-              if (nb + i < p.N) {
-                const float d = v[i] - st_shift;
-                st_s1 += d;
-                st_s2 = fmaf(d, d, st_s2);
-                ++st_cnt;
-              }
-            }
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && m0 < p.M) {
+            tma_store_2d(&tmY, box, n0, m0);
+            bulk_commit();
           }
         }
-        if (lane == 0) bulk_wait_read<0>();  // the previous store has read the box
-        __syncwarp();
-        uint8_t* box = stg;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          *reinterpret_cast<uint4*>(box + sw128_off(lane, q)) = pack8(v + 8 * q);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && m0 < p.M && nb < p.N) {
-          tma_store_2d(&tmY, box, nb, m0);
-          bulk_commit();
-        }
+        if (c + 1 < NCH) tc_wait_ld();
       }
       if (FUSE == gemm::FUSE_NORM && tile + (int)gridDim.x < num_tiles) {
 #pragma unroll
@@ -389,7 +413,8 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 }
 
 // Instantiated combinations: a folded LayerNorm feeds only bf16 (N, K) weights
-// with a store or GELU epilogue; statistics come only from residual epilogues.
+// with a store or GELU epilogue; statistics come only from bf16 residual
+// epilogues.
 template <int BN, int WMODE>
 int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb,
                  const CUtensorMap& ty, const GemmArgs& a, cudaStream_t st) {
@@ -404,7 +429,9 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
     return CK_ERR_UNSUPPORTED;
   }
   if (fuse == FUSE_STATS) {
-    if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty, a, st);
+    if constexpr (WMODE != W_I8_NK) {
+      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty, a, st);
+    }
     return CK_ERR_UNSUPPORTED;
   }
   switch (epi) {
@@ -492,7 +519,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   CUtensorMap ta, tb, ty;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
     return CK_ERR_INVALID_ARG;
-  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 64, 32, 128))
+  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 32, 32, 64))
     return CK_ERR_INVALID_ARG;
   bool ok;
   if (w_dtype == CK_I8) {

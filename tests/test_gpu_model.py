@@ -216,11 +216,12 @@ def test_norm_fold_matches_separate_norms(monkeypatch, name):
     assert _rel(folded, ref) <= TOL["bfloat16"], _rel(folded, ref)
 
 
-def test_norm_fold_follows_inplace_parameter_updates():
+def test_norm_fold_follows_inplace_parameter_updates(monkeypatch):
     """The folded weights are derived data: an in-place update of a norm or a
     linear weight (version counter) rebuilds them before the next forward."""
     from cortex.workloads import make_inputs
 
+    monkeypatch.setenv("CK_NORM_FOLD", "1")
     wl, model = _model("cfg1")
     inp, _ = make_inputs(wl, seed=7, batch=4)
     cols = ("neuron_ids", "time_bins", "values", "batch_indices")
