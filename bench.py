@@ -29,9 +29,7 @@ import datetime
 import json
 import math
 import os
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -65,57 +63,87 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples while the timed region runs."""
+    """SM clock and throttle reasons sampled every few milliseconds through NVML
+    while the timed region runs (nvidia-smi's 200 ms loop would see at most one
+    sample of a sub-second timed region); nvidia-smi is the fallback."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event-reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+    def __init__(self, device_index: int, interval_s: float = 0.005):
+        self.dev = device_index
+        self.interval = interval_s
+        self.samples = []
+        self.max_mhz = None
+        self.err = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+
+        try:
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = self.dev
+            if vis:
+                try:
+                    idx = int(vis.split(",")[self.dev])
+                except (ValueError, IndexError):
+                    pass
+            return pynvml.nvmlDeviceGetHandleByIndex(idx)
 
     def start(self):
+        import threading
+
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = self._handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report it instead of guessing
+            self.err = f"nvml unavailable: {type(e).__name__}"
+            return
+        self._stop = threading.Event()
+        first = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((mhz, rs))
+                except Exception as e:
+                    self.err = f"nvml sample failed: {type(e).__name__}"
+                first.set()
+                time.sleep(self.interval)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        first.wait(timeout=2.0)  # sampling is live before the timed region starts
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.fh.close()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() in ("active", "1"):
-                    reasons.add(n)
-        os.unlink(self.path)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self._thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "unavailable"]}
+        self._stop.set()
+        self._thread.join(timeout=2.0)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz,
+                    "reasons": [self.err or "no samples"]}
+        mhz = sorted(m for m, _ in self.samples)
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz), "source": "nvml"}
 
 
 def dist_env():
@@ -408,8 +436,8 @@ def run_ours(args, wl):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=25)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="cfg1")
     ap.add_argument("--no-graph", action="store_true")

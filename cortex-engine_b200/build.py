@@ -32,6 +32,7 @@ SOURCES = [
     "gemm_tc.cu",
     "gemm_simt.cu",
     "attention_tc.cu",
+    "attention_ws.cu",
     "attention_simt.cu",
     "capi.cu",
     "head.cu",

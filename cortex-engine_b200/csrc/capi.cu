@@ -38,6 +38,7 @@ int attention_dispatch(const ck_attention_args& a, cudaStream_t st) {
   if (a.key_offsets == nullptr && a.n_keys < 0) return CK_ERR_INVALID_ARG;
   if (a.block_mask != nullptr && (a.block_l <= 0 || a.block_e <= 0 || a.n_k_tiles < 0))
     return CK_ERR_INVALID_ARG;
+  if (attention_ws_supported(a)) return attention_ws(a, st);
   if (attention_tc_supported(a)) return attention_tc(a, st);
   return attention_simt(a, st);
 }

@@ -75,6 +75,9 @@ int gemm_simt(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const
 bool attention_tc_supported(const ck_attention_args& a);
 int attention_tc(const ck_attention_args& a, cudaStream_t st);
 int attention_simt(const ck_attention_args& a, cudaStream_t st);
+// warp-specialised persistent variant for unmasked bf16 head_dim 64 (attention_ws.cu)
+bool attention_ws_supported(const ck_attention_args& a);
+int attention_ws(const ck_attention_args& a, cudaStream_t st);
 
 // row norm (norm.cu)
 int row_norm(const void* x, int dtype, int64_t M, int32_t D, int64_t ldx, const void* gamma,
