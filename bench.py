@@ -38,6 +38,10 @@ for _p in (ROOT, os.path.join(ROOT, "cortex-engine_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "decoded windows/sec (Cortex-S, 512 ev/sample) at 1/2/4/8 B200; p99 batch latency"
+# DRAM traffic of the mlp.0 + GELU GEMM launch (8192 x 512 x 2048, bf16 weights)
+# from one ncu capture on B200 (10.58 MB read + 0.17 MB written; the 32 MB
+# output is still in L2 when the kernel ends).
+GELU_GEMM_TRAFFIC_BYTES = 10_745_600
 UNIT = "windows/s"
 
 
@@ -423,7 +427,12 @@ def run_ours(args, wl):
                                f"{wkind} weights)",
                      "bound": "tensor", "achieved": round(achieved, 1), "peak": tf_burst,
                      "unit": "TFLOP/s", "frac": round(achieved / tf_burst, 4),
-                     "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
+                     "peak_kind": f"{peak_kind} bf16 burst",
+                     "traffic": GELU_GEMM_TRAFFIC_BYTES if wl.name == "cfg1" else None,
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + "
+                                     "dram__bytes_write.sum, one capture of this launch)",
+                     "algorithmic_bytes": int(2 * (shape[0] * shape[1] + shape[1] * shape[2]
+                                                   + shape[0] * shape[2])),
                      "avg_launch_us": round(avg_s * 1e6, 2)},
         "clocks": clocks,
         "gpu_launches": int(launches_per_fwd) * args.steps,
