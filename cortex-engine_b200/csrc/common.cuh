@@ -172,31 +172,51 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// GELU of a pair, x >= kGeluTail: the same A&S 7.1.28 evaluation as gelu_as,
-// arranged for fewer instructions. The polynomial runs on |x| with its
-// coefficients pre-scaled by 2^(-k/2) (erf's argument is x / sqrt 2) and by
-// 2^(1/16), so the 16th power of the reciprocal is t = (1 - erf(|x|/sqrt 2)) / 2
-// = Phi(-|x|) directly; then GELU(x) = x * (x >= 0 ? 1 - t : t).
-__device__ __forceinline__ void gelu_pair(float& a, float& b) {
-  const unsigned long long y = f2pk(fabsf(a), fabsf(b));
-  unsigned long long q = ffma2(f2pk(5.6212996639622074e-06f, 5.6212996639622074e-06f), y,
-                               f2pk(5.1055209008659824e-05f, 5.1055209008659824e-05f));
-  q = ffma2(q, y, f2pk(3.96861370110139e-05f, 3.96861370110139e-05f));
-  q = ffma2(q, y, f2pk(3.422739238900824e-03f, 3.422739238900824e-03f));
-  q = ffma2(q, y, f2pk(2.2076998456581714e-02f, 2.2076998456581714e-02f));
-  q = ffma2(q, y, f2pk(5.207516303663057e-02f, 5.207516303663057e-02f));
-  q = ffma2(q, y, f2pk(1.0442737824274138f, 1.0442737824274138f));
-  float qa, qb;
-  f2up(q, qa, qb);
-  unsigned long long t = f2pk(rcp_approx(qa), rcp_approx(qb));
-  t = fmul2(t, t);
-  t = fmul2(t, t);
-  t = fmul2(t, t);
-  t = fmul2(t, t);
-  float ta, tb;
-  f2up(t, ta, tb);
-  const unsigned long long phi = f2pk(a >= 0.f ? 1.f - ta : ta, b >= 0.f ? 1.f - tb : tb);
-  f2up(fmul2(f2pk(a, b), phi), a, b);
+// GELU of 32 values, each >= kGeluTail: the same A&S 7.1.28 evaluation as
+// gelu_as, arranged for the issue rate of the epilogue warps. The polynomial
+// runs on |x| with its coefficients pre-scaled by 2^(-k/2) (erf's argument is
+// x / sqrt 2) and by 2^(1/16), so the 16th power of the reciprocal is
+// t = (1 - erf(|x|/sqrt 2)) / 2 directly; then GELU(x) = x Phi(x) =
+// x / 2 + |x| (1/2 - t) for either sign of x, with no select. The 16 value
+// pairs go through each step together (paired fp32 instructions), so every
+// step has 16 independent operations to hide the latency of the previous one.
+__device__ __forceinline__ void gelu32_pairs(float* v) {
+  unsigned long long y[16], q[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) y[i] = f2pk(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    q[i] = ffma2(f2pk(5.6212996639622074e-06f, 5.6212996639622074e-06f), y[i],
+                 f2pk(5.1055209008659824e-05f, 5.1055209008659824e-05f));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) q[i] = ffma2(q[i], y[i], f2pk(3.96861370110139e-05f, 3.96861370110139e-05f));
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    q[i] = ffma2(q[i], y[i], f2pk(3.422739238900824e-03f, 3.422739238900824e-03f));
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    q[i] = ffma2(q[i], y[i], f2pk(2.2076998456581714e-02f, 2.2076998456581714e-02f));
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    q[i] = ffma2(q[i], y[i], f2pk(5.207516303663057e-02f, 5.207516303663057e-02f));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) q[i] = ffma2(q[i], y[i], f2pk(1.0442737824274138f, 1.0442737824274138f));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float qa, qb;
+    f2up(q[i], qa, qb);
+    q[i] = f2pk(rcp_approx(qa), rcp_approx(qb));
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = fmul2(q[i], q[i]);
+  const unsigned long long half = f2pk(0.5f, 0.5f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const unsigned long long h = ffma2(q[i], f2pk(-1.f, -1.f), half);  // erf(|x|/sqrt 2) / 2
+    f2up(ffma2(y[i], h, fmul2(f2pk(v[2 * i], v[2 * i + 1]), half)), v[2 * i], v[2 * i + 1]);
+  }
 }
 
 // Kept out of line so that the compiler cannot if-convert the rare tail path
@@ -220,7 +240,7 @@ __device__ __forceinline__ void gelu32(float* v) {
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) gelu_pair(v[i], v[i + 1]);
+    gelu32_pairs(v);
   }
 }
 

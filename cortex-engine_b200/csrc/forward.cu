@@ -43,7 +43,7 @@ struct Layout {
 
 // Per-row LayerNorm statistics segments of a (., D) residual GEMM output.
 int64_t stats_segments(int64_t D) {
-  const int64_t sw = gemm_tc_block_n(D) / 2;
+  const int64_t sw = gemm_tc_stats_width(D, CK_BF16);
   return (D + sw - 1) / sw;
 }
 
@@ -137,7 +137,7 @@ int lin_stats(const ck_model* m, const void* A, int64_t M, int64_t K, const ck_l
 
 int lin_folded(const void* A, int64_t M, int64_t K, const ck_norm_fold& f, int64_t N, int epi,
                const void* stats, void* Y, cudaStream_t st) {
-  GemmFusion fz = {nullptr, stats, gemm_tc_block_n(K) / 2, 1e-5f, f.colsum, f.bias};
+  GemmFusion fz = {nullptr, stats, gemm_tc_stats_width(K, CK_BF16), 1e-5f, f.colsum, f.bias};
   return gemm_tc(A, M, K, K, f.w, CK_BF16, CK_W_NK, N, K, nullptr, epi, nullptr, 0, 0, Y, N, st,
                  &fz);
 }

@@ -11,14 +11,15 @@
 // Structure (one persistent CTA per SM, warp-specialised):
 //   warp 0       TMA producer: A and B tiles into a STAGES-deep smem ring
 //   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..9   epilogue: two warps per TMEM lane quarter, each taking half of
-//                the tile's columns in 32-column chunks: tcgen05.ld of the fp32
+//   warps 2..17  epilogue (2..9 in int8 mode): four (two) warps per TMEM lane
+//                quarter, each taking a quarter (half) of the tile's columns in
+//                32-column chunks: tcgen05.ld of the fp32
 //                accumulator (the next chunk's read and residual load in flight
 //                while the current one is finished), the epilogue op (folded
 //                norm, scale, bf16 rounding, GELU / residual / bias, row
-//                statistics), a 64B-swizzled 32 x 32 smem box per chunk (two
-//                per warp, alternating) and one TMA tile store per chunk
-//   warps 10..13 (int8 only) int8 -> bf16 converter
+//                statistics), a 64B-swizzled 32 x 32 smem box per chunk and
+//                one TMA tile store per chunk
+//   warps 18..21 (int8 only: 10..13) int8 -> bf16 converter
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1. All mbarrier waits are bounded
 // (common.cuh); a timeout raises a CTA-wide abort flag and every role drains.
@@ -38,24 +39,30 @@ using gemm::epilogue_math;
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
-constexpr int EPI_WARPS = 8;
 constexpr int STG_BOX = 32 * 32 * 2;  // one 32-row x 32-col bf16 store box (64B rows)
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
-template <int BN, int WMODE, int FUSE = 0>
+template <int BN, int WMODE, int FUSE = 0, int EPI = CK_EPI_STORE>
 struct GemmCfg {
+  // epilogue warps: four per TMEM lane quarter for the GELU epilogue with bf16
+  // weights, whose arithmetic per element is heavy enough that two warps per
+  // scheduler cannot keep up with the tensor cores; two per quarter otherwise
+  // (and always in int8 mode, whose converter warps need the registers)
+  static constexpr int EPI_WARPS = (WMODE != W_I8_NK && EPI == CK_EPI_GELU) ? 16 : 8;
+  static constexpr int EPI_GROUPS = EPI_WARPS / 4;  // column slices of a tile
+  static constexpr int EPI_COLS = BN / EPI_GROUPS;  // columns per epilogue warp per tile
   static constexpr int A_BYTES = BM * BK * 2;                        // 16 KB
   static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
   static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
   // per epilogue warp: two 32-row x 32-column bf16 store boxes (64B-swizzled)
-  static constexpr int STG_WARP = 2 * STG_BOX;
+  static constexpr int STG_WARP = (EPI_WARPS == 8 ? 2 : 1) * STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
   static constexpr int BAR_BYTES = 256;
   // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
   // one buffer per TMEM accumulator, so the epilogue reads them at smem latency
-  static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * (BN / 2) * 8 : 0;
+  static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * EPI_COLS * 8 : 0;
   static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
@@ -67,10 +74,10 @@ struct GemmCfg {
 };
 
 template <int BN, int WMODE, int EPI, int FUSE>
-__global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmY, const GemmArgs p) {
-  using C = GemmCfg<BN, WMODE, FUSE>;
+  using C = GemmCfg<BN, WMODE, FUSE, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -101,7 +108,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], EPI_WARPS * 32);
+      mbar_init(&tempty[a], C::EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -205,12 +212,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
       mbar_wait(drain, 0, nullptr, 8);
     }
   } else if (warp < C::CONV_WARP0) {
-    // ── epilogue: 8 warps, (lane quarter, column half) each ──
+    // ── epilogue: (lane quarter, column slice) per warp ──
     const int e = warp - 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int half = e >> 2;
+    const int half = e >> 2;       // column slice
     const int row = quarter * 32 + lane;
-    constexpr int NCH = BN / 64;  // 32-column chunks per warp per tile
+    constexpr int COLS = C::EPI_COLS;
+    constexpr int NCH = COLS / 32;  // 32-column chunks per warp per tile
+    constexpr int NBOX = C::STG_WARP / STG_BOX;
     uint8_t* stg = sStg + e * C::STG_WARP;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -218,14 +227,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
     // terms are fetched while the current tile is processed (registers for the
     // statistics, this warp's sFold[e][acc ^ 1] for its columns), so their
     // global latency stays off the per-tile chain. Warp-private: no barrier.
-    constexpr int FPL = (BN / 2) / 32;  // fold columns per lane
-    float2* wfold = sFold + e * BN;     // [2][BN / 2]
+    constexpr int FPL = COLS / 32;         // fold columns per lane
+    float2* wfold = sFold + e * 2 * COLS;  // [2][COLS]
     gemm::StatsRow srow;
     float2 fold_next[FPL];
     auto fetch_fold = [&](int t) {
 #pragma unroll
       for (int j = 0; j < FPL; ++j) {
-        const int n = (t / p.num_m_tiles) * BN + half * (BN / 2) + j * 32 + lane;
+        const int n = (t / p.num_m_tiles) * BN + half * COLS + j * 32 + lane;
         fold_next[j] = n < p.N ? make_float2(__ldg(p.fold_cs + n), __ldg(p.fold_bw + n))
                                : make_float2(0.f, 0.f);
       }
@@ -255,7 +264,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
       const int m = mt * BM + row;
       float st_shift = 0.f, st_s1 = 0.f, st_s2 = 0.f;  // segment statistics (FUSE_STATS)
       int st_cnt = 0;
-      const int col0 = half * (BN / 2);
+      const int col0 = half * COLS;
       const int nbase = nt * BN + col0;
       const uint32_t tbase =
           tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + col0);
@@ -269,9 +278,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
       // been read.
       float va[32], vb[32];
       uint4 ra[4], rb[4];
-      // (the int8 variant, short of registers beside its converter warps, reads
-      // the residual inside the epilogue math instead)
-      constexpr bool kPrefetch = EPI == CK_EPI_RESID && WMODE != W_I8_NK;
+      // (only the bf16 mode with two warps per lane quarter prefetches: with
+      // four warps the other warps hide the load, and the registers are short)
+      constexpr bool kPrefetch = EPI == CK_EPI_RESID && WMODE != W_I8_NK && C::EPI_WARPS == 8;
       auto fetch_res = [&](int c, uint4* dst) {
         if (kPrefetch && row_ok && nbase + c * 32 + 32 <= p.N) {
 #pragma unroll
@@ -279,26 +288,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
             dst[q] = __ldg(reinterpret_cast<const uint4*>(rrow + nbase + c * 32) + q);
         }
       };
+      // Two warps per lane quarter read ahead (double-buffered chunks); with
+      // four, each warp reads a chunk when it needs it and the other warps of
+      // its scheduler cover the latency, which keeps it inside 96 registers.
+      constexpr bool kAhead = C::EPI_WARPS == 8;
       tmem_ld32(tbase, va);
       fetch_res(0, ra);
       tc_wait_ld();
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
-        float* cur = (c & 1) ? vb : va;
+        float* cur = (kAhead && (c & 1)) ? vb : va;
         float* nxt = (c & 1) ? va : vb;
         uint4* rcur = (c & 1) ? rb : ra;
         uint4* rnxt = (c & 1) ? ra : rb;
-        if (c + 1 < NCH) {
+        if (!kAhead && c > 0) {
+          tmem_ld32(tbase + (uint32_t)(c * 32), va);
+          tc_wait_ld();
+        }
+        if (kAhead && c + 1 < NCH) {
           tmem_ld32(tbase + (uint32_t)((c + 1) * 32), nxt);
           fetch_res(c + 1, rnxt);
-        } else {
+        } else if (c + 1 == NCH) {
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
         const int n0 = nbase + c * 32;
         if (n0 < p.N) {
           uint32_t packed[16];
-          epilogue_math<EPI, FUSE>(p, m, n0, cur, nmean, nrstd, wfold + acc * (BN / 2) + c * 32,
+          epilogue_math<EPI, FUSE>(p, m, n0, cur, nmean, nrstd, wfold + acc * COLS + c * 32,
                                    (kPrefetch && n0 + 32 <= p.N) ? rcur : nullptr, packed);
           if (FUSE == gemm::FUSE_STATS) {
             // statistics of the values as stored (bf16), shifted by the
@@ -326,8 +343,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
           }
           // 64B-swizzled 32 x 32 box, then one TMA store per chunk; the box was
           // last read by the store issued two chunks ago
-          uint8_t* box = stg + (c & 1) * STG_BOX;
-          if (lane == 0) bulk_wait_read<1>();
+          // the box is free once the store that last used it has read it
+          uint8_t* box = stg + (NBOX == 2 ? (c & 1) : 0) * STG_BOX;
+          if (lane == 0) {
+            if (NBOX == 2)
+              bulk_wait_read<1>();
+            else
+              bulk_wait_read<0>();
+          }
           __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -340,11 +363,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
             bulk_commit();
           }
         }
-        if (c + 1 < NCH) tc_wait_ld();
+        if (kAhead && c + 1 < NCH) tc_wait_ld();
       }
       if (FUSE == gemm::FUSE_NORM && tile + (int)gridDim.x < num_tiles) {
 #pragma unroll
-        for (int j = 0; j < FPL; ++j) wfold[(acc ^ 1) * (BN / 2) + j * 32 + lane] = fold_next[j];
+        for (int j = 0; j < FPL; ++j) wfold[(acc ^ 1) * COLS + j * 32 + lane] = fold_next[j];
       }
       if (FUSE == gemm::FUSE_STATS && m < p.M && st_cnt > 0) {
         const int seg = (nt * BN + col0) / p.stats_sw;
@@ -402,7 +425,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE>::NUM_THREADS, 1)
 template <int BN, int WMODE, int EPI, int FUSE>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
                 const GemmArgs& a, cudaStream_t st) {
-  using C = GemmCfg<BN, WMODE, FUSE>;
+  using C = GemmCfg<BN, WMODE, FUSE, EPI>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
   auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
@@ -469,6 +492,12 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
 
 int gemm_tc_block_n(int64_t N) { return (N % 256 == 0 || N > 256) ? 256 : 128; }
 
+int gemm_tc_stats_width(int64_t N, int w_dtype) {
+  const int BN = gemm_tc_block_n(N);
+  return w_dtype == CK_I8 ? BN / GemmCfg<256, W_I8_NK, 2, CK_EPI_RESID>::EPI_GROUPS
+                          : BN / GemmCfg<256, W_BF16_NK, 2, CK_EPI_RESID>::EPI_GROUPS;
+}
+
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
             int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st,
@@ -488,7 +517,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   if (w_dtype == CK_I8 && w_scale == nullptr) return CK_ERR_INVALID_ARG;
   a.scale_vec = (reinterpret_cast<uintptr_t>(w_scale) & 15u) == 0;
   a.stats_out = nullptr;
-  a.stats_sw = BN / 2;
+  a.stats_sw = gemm_tc_stats_width(N, w_dtype);
   a.stats_in = nullptr;
   a.stats_in_sw = 0;
   a.stats_in_nseg = 0;

@@ -47,7 +47,7 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
                        int epi, const void* aux, int64_t ld_aux);
 // Optional epilogue fusions of the tcgen05 GEMM (see gemm_common.cuh):
 //   stats_out  residual epilogue also writes per-row, per-segment (mean, M2)
-//              of its output, segment width gemm_tc_block_n(N) / 2
+//              of its output, segment width gemm_tc_stats_width(N, w_dtype)
 //   stats_in   LayerNorm folded into this GEMM: A is the raw residual, W is
 //              W * gamma, fold_cs[n] = sum_k W[n,k] * gamma[k] (as stored),
 //              fold_bw[n] = sum_k W[n,k] * beta[k]
@@ -60,6 +60,7 @@ struct GemmFusion {
   const float* fold_bw;
 };
 int gemm_tc_block_n(int64_t N);
+int gemm_tc_stats_width(int64_t N, int w_dtype);  // column width of one statistics segment
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
             int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st,
