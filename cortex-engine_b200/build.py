@@ -39,6 +39,8 @@ SOURCES = [
     "fold.cu",
     "forward.cu",
     "noalloc.cu",
+    "batch.cpp",
+    "ingest.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -62,13 +64,20 @@ def _deps_mtime() -> float:
     return max(os.path.getmtime(p) for p in paths)
 
 
+# Host-only sources (.cpp) go to the host compiler directly.
+HOST_CFLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-I", INCLUDE, "-I", CSRC]
+
+
 def _compile(src: str, force: bool, extra: list[str]) -> str:
-    obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
     srcp = os.path.join(CSRC, src)
     if (not force and os.path.exists(obj)
             and os.path.getmtime(obj) >= max(os.path.getmtime(srcp), _deps_mtime())):
         return obj
-    cmd = [nvcc()] + CFLAGS + extra + ["-c", srcp, "-o", obj]
+    if src.endswith(".cpp"):
+        cmd = [shutil.which("g++") or "g++"] + HOST_CFLAGS + ["-c", srcp, "-o", obj]
+    else:
+        cmd = [nvcc()] + CFLAGS + extra + ["-c", srcp, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")

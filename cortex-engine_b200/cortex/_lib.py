@@ -123,7 +123,19 @@ _SIGS = {
     "ck_forward_workspace_bytes": (_sz, [ctypes.POINTER(Model), _i64, _i32]),
     "ck_forward": (_int, [ctypes.POINTER(Model), _vp, _vp, _vp, _vp, _int, _i64, _i32, _vp, _vp,
                           _sz, _vp]),
+    "ck_batch_stage": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _vp, _i64,
+                              ctypes.POINTER(_i32)]),
+    "ck_forward_batch": (_int, [ctypes.POINTER(Model), _vp, _i64, _i32, _vp, _vp, _sz, _vp]),
+    "ck_collate_bins_workspace_bytes": (_sz, [_i32, _i32]),
+    "ck_collate_bins": (_int, [_vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _sz, _vp, _vp]),
 }
+
+CK_BATCH_HEADER_WORDS = 4
+
+
+def batch_words(capacity: int) -> int:
+    """int32 words of a packed event batch (CK_BATCH_WORDS in cortex_b200.h)."""
+    return CK_BATCH_HEADER_WORDS + 4 * capacity
 
 EXPORTED_SYMBOLS = tuple(_SIGS)
 

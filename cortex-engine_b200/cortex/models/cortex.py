@@ -6,8 +6,10 @@ order and ``forward`` signature (cortex/models/cortex.py:72-122). With
 graph to ``ck_forward``: packing, tokenizer with the fused norm_kv, batch-
 invariant latent queries, packed varlen cross-attention, the self-attention
 stack and the behaviour head, launched back to back on the current stream with
-no host synchronisation inside. Index tensors may be on the host (they are
-copied to the model's device, asynchronously when pinned) or on the device.
+no host synchronisation inside. Index tensors may be on the device, or on
+the host: then they go through ``cortex.batching`` -- one packed int32 batch in
+pinned memory, one copy to the device and the replay of a CUDA graph captured
+for the batch's (B, event-capacity) bucket.
 
 ``_pack_events`` keeps the reference's padded-output contract
 (cortex/models/cortex.py:125-165) on top of the device packing kernels.
@@ -16,6 +18,7 @@ copied to the model's device, asynchronously when pinned) or on the device.
 from __future__ import annotations
 
 import ctypes
+import operator
 import os
 import threading
 from typing import cast
@@ -86,6 +89,7 @@ class CortexModel(nn.Module):
         self._native_key = None
         self._native = None
         self._workspace: dict[torch.device, torch.Tensor] = {}
+        self._batch_runner = None
 
     # ── native graph description ────────────────────────────────────────────
 
@@ -122,19 +126,32 @@ class CortexModel(nn.Module):
 
     def _state_key(self):
         # Weight pointers only change through _apply / load_state_dict (both
-        # invalidate the cache) or by swapping submodules (convert_model), which
-        # changes the module identities checked here.
-        return tuple(id(m) for m in self.modules())
+        # invalidate the cache), by swapping submodules (convert_model) or by
+        # assigning new Parameters. The key is every (child dict, name) slot of
+        # the module tree with the identity of what it held at build time;
+        # checking it is one C-level pass (map) instead of a module walk.
+        dicts, names, objs = [], [], []
+        for mod in self.modules():
+            for d in (mod._modules, mod._parameters, mod._buffers):
+                for n, c in d.items():
+                    dicts.append(d)
+                    names.append(n)
+                    objs.append(c)  # held, so no later object can reuse its identity
+        return dicts, names, objs
+
+    def _state_unchanged(self) -> bool:
+        key = self._native_key
+        return key is not None and all(map(operator.is_, map(dict.get, key[0], key[1]), key[2]))
 
     def native_model(self) -> L.Model:
         """The ``ck_model`` description of this module's weights (cached).
 
         The description holds raw device pointers of the parameters; in-place
         updates of parameter values are seen by the next forward as they are."""
-        key = self._state_key()
         with self._native_lock:
-            if self._native is not None and self._native_key == key:
+            if self._native is not None and self._state_unchanged():
                 return self._native[0]
+            key = self._state_key()
             keep: list = []
             folds: list = []
             cfg = self.config
@@ -250,6 +267,21 @@ class CortexModel(nn.Module):
         """Drop the cached weight description (and the derived LayerNorm folds)."""
         self._native = None
 
+    def forward_packed(self, packed) -> dict[str, torch.Tensor]:
+        """``{"behavior": (B, behavior_dim)}`` for a ``cortex.data.PackedBatch``
+        already on the device (``collate_windows``): the batch's events never
+        leave HBM; one device copy and a graph replay of its bucket."""
+        return {"behavior": self.batch_runner().forward_batch(packed.batch, packed.capacity,
+                                                              packed.batch_size)}
+
+    def batch_runner(self):
+        """The packed-batch runner host-index forwards go through (cortex.batching)."""
+        if self._batch_runner is None:
+            from cortex.batching import BatchRunner
+
+            self._batch_runner = BatchRunner(self)
+        return self._batch_runner
+
     def workspace(self, device: torch.device, nbytes: int) -> torch.Tensor:
         ws = self._workspace.get(device)
         if ws is None or ws.numel() < nbytes:
@@ -278,6 +310,11 @@ class CortexModel(nn.Module):
                 f"values={values.shape}, batch_indices={batch_indices.shape}")
         dev = self.tokenizer.neuron_emb.weight.device
         L.require_cuda(self.tokenizer.neuron_emb.weight, what="CortexModel.forward")
+        if not return_aux and all(x.device.type == "cpu" for x in
+                                  (neuron_ids, time_bins, values, batch_indices)):
+            # host indices: one packed int32 batch, one copy, one graph replay
+            return {"behavior": self.batch_runner().forward_host(
+                neuron_ids, time_bins, values, batch_indices, batch_size)}
         E = int(batch_indices.shape[0])
         if batch_size is None:
             batch_size = int(batch_indices.max().item()) + 1 if E > 0 else 1

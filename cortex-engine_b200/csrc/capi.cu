@@ -49,11 +49,22 @@ extern "C" {
 
 size_t ck_pack_workspace_bytes(int64_t E, int32_t B) { return pack_workspace_bytes(E, B); }
 
+size_t ck_collate_bins_workspace_bytes(int32_t B, int32_t window_bins) {
+  return collate_bins_workspace_bytes(B, window_bins);
+}
+
+int ck_collate_bins(const ck_bin_window* windows, int32_t B, int32_t window_bins,
+                    int32_t n_buckets, int32_t max_neurons, int32_t* batch, int64_t capacity,
+                    void* workspace, size_t workspace_bytes, int32_t* n_total, void* stream) {
+  return collate_bins(windows, B, window_bins, n_buckets, max_neurons, batch, capacity, workspace,
+                      workspace_bytes, n_total, S(stream));
+}
+
 int ck_pack_events(const void* batch_indices, int idx_dtype, int64_t idx_stride, int64_t E,
                    int32_t B, int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* e_max,
                    void* workspace, size_t workspace_bytes, void* stream) {
-  return pack_events(batch_indices, idx_dtype, idx_stride, E, B, counts, offsets, dest, e_max,
-                     workspace, workspace_bytes, S(stream));
+  return pack_events(batch_indices, idx_dtype, idx_stride, E, B, nullptr, counts, offsets, dest,
+                     e_max, workspace, workspace_bytes, S(stream));
 }
 
 int ck_pack_scatter(const void* flat, int dtype, int64_t E, int32_t D, int64_t flat_stride,

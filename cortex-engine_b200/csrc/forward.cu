@@ -156,9 +156,13 @@ extern "C" size_t ck_forward_workspace_bytes(const ck_model* m, int64_t E, int32
   return plan(m, E, B).total + 256;
 }
 
-extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, const void* val,
-                          const void* bidx, int idx_dt, int64_t E, int32_t B, void* out, void* ws,
-                          size_t ws_bytes, void* stream) {
+namespace {
+
+// The forward over E events, of which events *n_valid..E-1 are padding when
+// n_valid (a device word) is given.
+int forward_impl(const ck_model* m, const void* nid, const void* tb, const void* val,
+                 const void* bidx, int idx_dt, int64_t E, int32_t B, const int32_t* n_valid,
+                 void* out, void* ws, size_t ws_bytes, void* stream) {
   if (m == nullptr || out == nullptr || B <= 0 || E < 0) return CK_ERR_INVALID_ARG;
   if (m->dtype != CK_BF16 && m->dtype != CK_F32) return CK_ERR_UNSUPPORTED;
   if (m->latent_dim <= 0 || m->hidden_dim <= 0 || m->num_latents <= 0 || m->num_heads <= 0 ||
@@ -191,12 +195,12 @@ extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, co
   } while (0)
 
   // 1. packing
-  CK_TRY(pack_events(bidx, idx_dt, 1, E, B, counts, offsets, dest, emax, P(lay.packws),
+  CK_TRY(pack_events(bidx, idx_dt, 1, E, B, n_valid, counts, offsets, dest, emax, P(lay.packws),
                      pack_workspace_bytes(E, B), st));
   // 2. tokenizer + norm_kv, written in packed order
   CK_TRY(tokenize(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din, m->n_vocab,
                   m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1, 1, 1, E, dest,
-                  m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st));
+                  m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st, n_valid));
   // 3. latent queries (batch-invariant)
   CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
                   CK_NORM_LAYER, P(lay.xq), D, st));
@@ -361,4 +365,21 @@ extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, co
              out, 1, st));
 #undef CK_TRY
   return CK_OK;
+}
+
+}  // namespace
+
+extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, const void* val,
+                          const void* bidx, int idx_dt, int64_t E, int32_t B, void* out, void* ws,
+                          size_t ws_bytes, void* stream) {
+  return forward_impl(m, nid, tb, val, bidx, idx_dt, E, B, nullptr, out, ws, ws_bytes, stream);
+}
+
+extern "C" int ck_forward_batch(const ck_model* m, const int32_t* batch, int64_t capacity,
+                                int32_t B, void* out, void* ws, size_t ws_bytes, void* stream) {
+  if (batch == nullptr || capacity < 0 || capacity % 4 != 0) return CK_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(batch) & 15u) != 0) return CK_ERR_INVALID_ARG;
+  const int32_t* a = batch + CK_BATCH_HEADER_WORDS;
+  return forward_impl(m, a, a + capacity, a + 2 * capacity, a + 3 * capacity, CK_I32, capacity, B,
+                      batch, out, ws, ws_bytes, stream);
 }

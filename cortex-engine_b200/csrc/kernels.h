@@ -90,9 +90,10 @@ int row_norm2(const void* x, int dtype, int64_t M, int32_t D, int64_t ldx, const
 
 // packing and tokenizer (pack.cu, tokenizer.cu)
 size_t pack_workspace_bytes(int64_t E, int32_t B);
+// n_valid (device, may be NULL): events n_valid..E-1 are padding (pack.cu)
 int pack_events(const void* bidx, int idx_dtype, int64_t idx_stride, int64_t E, int32_t B,
-                int32_t* counts, int32_t* offsets, int32_t* dest, int32_t* e_max, void* ws,
-                size_t ws_bytes, cudaStream_t st);
+                const int32_t* n_valid, int32_t* counts, int32_t* offsets, int32_t* dest,
+                int32_t* e_max, void* ws, size_t ws_bytes, cudaStream_t st);
 int pack_scatter(const void* flat, int dtype, int64_t E, int32_t D, int64_t flat_stride,
                  const void* bidx, int idx_dtype, int64_t idx_stride, const int32_t* dest,
                  const int32_t* offsets, int32_t e_max, void* out, uint8_t* mask,
@@ -102,7 +103,13 @@ int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
              int64_t v_ld, const void* nid, const void* tb, const void* val, int idx_dtype,
              int64_t s_nid, int64_t s_tb, int64_t s_val, int64_t E, const int32_t* dest,
              const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
-             cudaStream_t st);
+             cudaStream_t st, const int32_t* n_valid = nullptr);
+
+// event ingest from bin-count matrices (ingest.cu)
+size_t collate_bins_workspace_bytes(int32_t B, int32_t W);
+int collate_bins(const ck_bin_window* wins, int32_t B, int32_t W, int32_t n_buckets,
+                 int32_t max_neurons, int32_t* batch, int64_t capacity, void* ws, size_t ws_bytes,
+                 int32_t* n_total, cudaStream_t st);
 
 // behaviour head in algebraic form (head.cu): head_prep builds the weight-only
 // (NT, D) matrix once per forward, head_fused runs both LayerNorms, the

@@ -17,6 +17,11 @@
 //   5. dest     dest[e] = e for sorted input, else offsets + chunk prefix + rank
 // Sorted input -- what collate_events produces (cortex/data/nlb.py:492-512) --
 // skips steps 3-4 on the device (they exit on the flag).
+//
+// Padded batches: with n_valid != NULL only events 0..*n_valid-1 are real (the
+// count is read on the device, so one captured launch sequence serves every
+// batch of a capacity bucket). Padding events are not counted, and dest[e] = e
+// for them, which is a row no real event occupies.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -32,6 +37,13 @@ constexpr int64_t MAX_RANK_MATRIX = 16ll << 20;
 __device__ __forceinline__ int64_t load_idx(const void* p, int dt, int64_t i, int64_t stride) {
   if (dt == CK_I64) return reinterpret_cast<const int64_t*>(p)[i * stride];
   return (int64_t) reinterpret_cast<const int32_t*>(p)[i * stride];
+}
+
+// Number of real events: *n_valid clamped to [0, E], or E without a count.
+__device__ __forceinline__ int64_t real_events(const int32_t* n_valid, int64_t E) {
+  if (n_valid == nullptr) return E;
+  const int64_t nv = *n_valid;
+  return nv < 0 ? 0 : (nv > E ? E : nv);
 }
 
 struct PackWs {
@@ -58,13 +70,16 @@ PackWs carve(void* ws, int64_t E, int32_t B) {
 }
 
 __global__ void pack_count_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
-                                  int32_t* counts, int32_t* flag) {
+                                  const int32_t* n_valid, int32_t* counts, int32_t* flag) {
   grid_dep_wait();
   grid_dep_launch();
   const int lane = threadIdx.x & 31;
+  const int64_t nv = real_events(n_valid, E);
+  if (n_valid != nullptr && blockIdx.x == 0 && threadIdx.x == 0 && (*n_valid < 0 || *n_valid > E))
+    set_status(CK_ERR_INVALID_ARG, *n_valid, (int)E);
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e - lane < E;
        e += (int64_t)gridDim.x * blockDim.x) {
-    const bool in = e < E;
+    const bool in = e < nv;
     int64_t b = in ? load_idx(bidx, dt, e, stride) : -1;
     if (in && (b < 0 || b >= B)) {
       set_status(CK_ERR_INDEX, (int)e, (int)b);
@@ -135,7 +150,7 @@ __global__ void pack_scan_kernel(const int32_t* counts, int32_t B, int32_t* offs
 }
 
 __global__ void pack_rank_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
-                                 PackWs w) {
+                                 const int32_t* n_valid, PackWs w) {
   grid_dep_wait();
   grid_dep_launch();
   if (w.flag[0] == 0) return;  // sorted: ranks are not needed
@@ -148,7 +163,7 @@ __global__ void pack_rank_kernel(const void* bidx, int dt, int64_t stride, int64
   const int64_t c = blockIdx.x;
   const int64_t e = c * CHUNK + t;
   int32_t b = -1;
-  if (e < E) {
+  if (e < real_events(n_valid, E)) {
     int64_t v = load_idx(bidx, dt, e, stride);
     b = (v >= 0 && v < B) ? (int32_t)v : -1;
   }
@@ -202,12 +217,18 @@ __global__ void pack_colscan_kernel(PackWs w) {
 }
 
 __global__ void pack_dest_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
-                                 const int32_t* offsets, PackWs w, int32_t* dest) {
+                                 const int32_t* n_valid, const int32_t* offsets, PackWs w,
+                                 int32_t* dest) {
   grid_dep_wait();
   grid_dep_launch();
   const bool unsorted = w.flag[0] != 0;
+  const int64_t nv = real_events(n_valid, E);
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E;
        e += (int64_t)gridDim.x * blockDim.x) {
+    if (e >= nv) {  // padding: real events fill rows 0..nv-1
+      dest[e] = (int32_t)e;
+      continue;
+    }
     const int64_t v = load_idx(bidx, dt, e, stride);
     if (v < 0 || v >= B) {
       dest[e] = -1;
@@ -254,9 +275,9 @@ size_t pack_workspace_bytes(int64_t E, int32_t B) {
   return bytes;
 }
 
-int pack_events(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B, int32_t* counts,
-                int32_t* offsets, int32_t* dest, int32_t* e_max, void* ws, size_t ws_bytes,
-                cudaStream_t st) {
+int pack_events(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
+                const int32_t* n_valid, int32_t* counts, int32_t* offsets, int32_t* dest,
+                int32_t* e_max, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (E < 0 || B <= 0 || counts == nullptr || offsets == nullptr || e_max == nullptr)
     return CK_ERR_INVALID_ARG;
   if (E > 0 && (bidx == nullptr || dest == nullptr)) return CK_ERR_INVALID_ARG;
@@ -273,15 +294,15 @@ int pack_events(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B, 
   if (E > 0) {
     int64_t blocks = (E + 255) / 256;
     if (blocks > 8 * sms) blocks = 8 * sms;
-    if (launch_pdl(pack_count_kernel, dim3((unsigned)blocks), dim3(256), 0, st, bidx, dt, stride, E, B, counts, w.flag)) return CK_ERR_CUDA;
+    if (launch_pdl(pack_count_kernel, dim3((unsigned)blocks), dim3(256), 0, st, bidx, dt, stride, E, B, n_valid, counts, w.flag)) return CK_ERR_CUDA;
   }
   if (launch_pdl(pack_scan_kernel, dim3(1), dim3(1024), 0, st, counts, B, offsets, e_max)) return CK_ERR_CUDA;
   if (E > 0) {
-    if (launch_pdl(pack_rank_kernel, dim3((unsigned)w.nchunks), dim3(CHUNK), 0, st, bidx, dt, stride, E, B, w)) return CK_ERR_CUDA;
+    if (launch_pdl(pack_rank_kernel, dim3((unsigned)w.nchunks), dim3(CHUNK), 0, st, bidx, dt, stride, E, B, n_valid, w)) return CK_ERR_CUDA;
     if (launch_pdl(pack_colscan_kernel, dim3((unsigned)B), dim3(256), 0, st, w)) return CK_ERR_CUDA;
     int64_t blocks = (E + 255) / 256;
     if (blocks > 8 * sms) blocks = 8 * sms;
-    if (launch_pdl(pack_dest_kernel, dim3((unsigned)blocks), dim3(256), 0, st, bidx, dt, stride, E, B, offsets, w, dest)) return CK_ERR_CUDA;
+    if (launch_pdl(pack_dest_kernel, dim3((unsigned)blocks), dim3(256), 0, st, bidx, dt, stride, E, B, n_valid, offsets, w, dest)) return CK_ERR_CUDA;
   }
   return CK_OK;
 }

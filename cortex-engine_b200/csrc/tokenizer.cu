@@ -9,7 +9,10 @@
 // vectors of the three rows (4 vectors per lane per table at D = 512). With gamma != NULL the finished row is LayerNorm-ed in
 // registers before the store, which fuses CrossAttentionBlock.norm_kv
 // (cortex/models/perceiver.py:68) into the gather: the raw tokens never reach HBM.
-// Out-of-range indices set CK_ERR_INDEX and write a zero row.
+// Out-of-range indices set CK_ERR_INDEX and write a zero row. With n_valid set
+// (device count, padded batches) events n_valid..E-1 are padding: their ids
+// are not read and their rows are written as zeros, which keeps every row a
+// later kernel may touch finite.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -63,6 +66,7 @@ struct TokArgs {
   void* out;
   int64_t out_ld;
   int D;
+  const int32_t* n_valid;
 };
 
 // G lanes share one event row (G in {8, 16, 32}, so a warp handles 32 / G
@@ -84,12 +88,14 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
   const T* ve = reinterpret_cast<const T*>(a.v_emb);
   T* out = reinterpret_cast<T*>(a.out);
   const int nvec = a.D / VEC;
+  const int64_t nv = a.n_valid ? min((int64_t)max(*a.n_valid, 0), a.E) : a.E;
   for (int64_t base = warp * RPW; base < a.E; base += nwarps * RPW) {
     const int64_t e = base + slot;
     const bool live = e < a.E;
+    const bool real = e < nv;
     int64_t dst_row = -1, n = 0, t = 0, v = 0;
-    if (live) {
-      dst_row = a.dest ? (int64_t)a.dest[e] : e;
+    if (live) dst_row = a.dest ? (int64_t)a.dest[e] : e;
+    if (real) {
       n = load_idx(a.nid, a.idx_dt, e, a.s_nid);
       t = load_idx(a.tb, a.idx_dt, e, a.s_tb);
       v = load_idx(a.val, a.idx_dt, e, a.s_val);
@@ -97,8 +103,8 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
     const bool in_range =
         n >= 0 && n < a.n_vocab && t >= 0 && t < a.t_vocab && v >= 0 && v < a.v_vocab;
     const bool store = live && dst_row >= 0;
-    const bool ok = store && in_range;
-    if (store && !in_range && sub == 0)
+    const bool ok = store && real && in_range;
+    if (store && real && !in_range && sub == 0)
       set_status(CK_ERR_INDEX, (int)e,
                  (int)(n < 0 || n >= a.n_vocab ? n : (t < 0 || t >= a.t_vocab ? t : v)));
     float x[MAXV][VEC];
@@ -227,13 +233,13 @@ int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
              int64_t v_ld, const void* nid, const void* tb, const void* val, int idx_dtype,
              int64_t s_nid, int64_t s_tb, int64_t s_val, int64_t E, const int32_t* dest,
              const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
-             cudaStream_t st) {
+             cudaStream_t st, const int32_t* n_valid) {
   if (E == 0) return CK_OK;
   if (E < 0 || D <= 0 || !n_emb || !t_emb || !v_emb || !nid || !tb || !val || !out)
     return CK_ERR_INVALID_ARG;
   if (idx_dtype != CK_I64 && idx_dtype != CK_I32) return CK_ERR_UNSUPPORTED;
   TokArgs a{n_emb, t_emb, v_emb, n_vocab, t_vocab, v_vocab, n_ld, t_ld, v_ld, nid, tb, val,
-            idx_dtype, s_nid, s_tb, s_val, E, dest, gamma, beta, eps, out, out_ld, D};
+            idx_dtype, s_nid, s_tb, s_val, E, dest, gamma, beta, eps, out, out_ld, D, n_valid};
   const int es = dtype == CK_F32 ? 4 : 2;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const bool vec_ok = ((int64_t)D * es) % 16 == 0 && (n_ld * es) % 16 == 0 &&

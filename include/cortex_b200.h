@@ -242,6 +242,65 @@ int ck_forward(const ck_model* m, const void* neuron_ids, const void* time_bins,
                int32_t B, void* behavior_out, void* workspace, size_t workspace_bytes,
                void* stream);
 
+/* ── packed event batches ─────────────────────────────────────────────────
+ * One batch of events in one int32 buffer, so that a batch crosses to the
+ * device in a single copy and one captured launch sequence serves every batch
+ * with the same (B, capacity):
+ *
+ *   int32 n_valid, reserved[3];
+ *   int32 neuron_ids[capacity], time_bins[capacity], values[capacity],
+ *         batch_indices[capacity];
+ *
+ * capacity is a multiple of 4, so every array starts 16-byte aligned. Events
+ * n_valid..capacity-1 are padding; their entries are never read. The buffer
+ * replaces the per-request list building and the four int64 tensors of
+ * InferenceWorker._run_batch_sync (cortex/serve/worker.py:166-200). */
+#define CK_BATCH_HEADER_WORDS 4
+#define CK_BATCH_WORDS(capacity) (CK_BATCH_HEADER_WORDS + 4 * (int64_t)(capacity))
+
+/* HOST memory only, no device work. Writes E events from four host index
+ * arrays (idx_dtype CK_I32 or CK_I64, unit stride) into a batch buffer:
+ * n_valid = E, ids narrowed to int32 (saturating, so an id outside int32
+ * stays out of its table and the device reports CK_ERR_INDEX, where the
+ * reference's embedding lookup raises), and *batch_size = max(batch_indices)
+ * + 1, the B of cortex/models/cortex.py:137 (1 when E == 0). Returns
+ * CK_ERR_INDEX for a negative batch index or one that does not fit int32
+ * (torch.bincount rejects negative input, cortex/models/cortex.py:141). */
+int ck_batch_stage(const void* neuron_ids, const void* time_bins, const void* values,
+                   const void* batch_indices, int idx_dtype, int64_t E, int32_t* batch,
+                   int64_t capacity, int32_t* batch_size);
+
+/* ck_forward over a device batch buffer (16-byte aligned): capacity event
+ * slots, of which the first n_valid (read on the device) are events. Size the
+ * workspace with ck_forward_workspace_bytes(m, capacity, B). */
+int ck_forward_batch(const ck_model* m, const int32_t* batch, int64_t capacity, int32_t B,
+                     void* behavior_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ── event ingest from bin-count matrices ─────────────────────────────────
+ * events_from_bin_matrix + bucket_values + collate_events
+ * (cortex/data/nlb.py:74-114, 249-280, 492-512) on the device: B windows of
+ * window_bins rows each, every nonzero bin one event, in (window, time bin,
+ * neuron) order, written as a packed event batch. */
+typedef struct {
+  const int32_t* counts; /* (n_rows, ld) int32 spike counts of one session, device */
+  int64_t ld;            /* row stride in elements (>= n_neurons) */
+  int64_t n_rows;        /* rows (time bins) of the matrix */
+  int64_t start;         /* first row of the window */
+  int32_t n_neurons;     /* columns (units of the session) */
+  int32_t neuron_offset; /* added to the column (SessionData.neuron_id_offset) */
+} ck_bin_window;
+
+size_t ck_collate_bins_workspace_bytes(int32_t B, int32_t window_bins);
+/* windows: (B,) ck_bin_window in device memory. Writes the batch (capacity
+ * slots, n_valid = min(events, capacity)) and, when n_total != NULL, the
+ * uncapped event count to the device int32 *n_total. Events past capacity
+ * are dropped and record CK_ERR_INVALID_ARG; capacity 0 only counts (the
+ * batch needs its header words only). A neuron id >= max_neurons or a window
+ * outside its matrix records CK_ERR_INDEX (the window is skipped). */
+int ck_collate_bins(const ck_bin_window* windows, int32_t B, int32_t window_bins,
+                    int32_t n_buckets, int32_t max_neurons, int32_t* batch, int64_t capacity,
+                    void* workspace, size_t workspace_bytes, int32_t* n_total, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,3 +38,8 @@ def golden_kernels():
 @pytest.fixture(scope="session")
 def golden_models():
     return torch.load(os.path.join(GOLDEN, "golden_models.pt"), weights_only=False)
+
+
+@pytest.fixture(scope="session")
+def golden_ingest():
+    return torch.load(os.path.join(GOLDEN, "golden_ingest.pt"), weights_only=False)
