@@ -41,6 +41,7 @@ SOURCES = [
     "noalloc.cu",
     "batch.cpp",
     "ingest.cu",
+    "rows.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -126,6 +126,10 @@ _SIGS = {
     "ck_batch_stage": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _vp, _i64,
                               ctypes.POINTER(_i32)]),
     "ck_forward_batch": (_int, [ctypes.POINTER(Model), _vp, _i64, _i32, _vp, _vp, _sz, _vp]),
+    "ck_forward_kv": (_int, [ctypes.POINTER(Model), _vp, _i64, _i32, _vp, _vp, _vp, _sz, _vp]),
+    "ck_forward_from_kv": (_int, [ctypes.POINTER(Model), _vp, _i64, _vp, _i32, _vp, _vp, _sz,
+                                  _vp]),
+    "ck_copy_rows": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _i32, _vp]),
     "ck_collate_bins_workspace_bytes": (_sz, [_i32, _i32]),
     "ck_collate_bins": (_int, [_vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _sz, _vp, _vp]),
 }

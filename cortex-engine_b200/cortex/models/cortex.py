@@ -274,6 +274,15 @@ class CortexModel(nn.Module):
         return {"behavior": self.batch_runner().forward_batch(packed.batch, packed.capacity,
                                                               packed.batch_size)}
 
+    def forward_streaming(self, windows: list[dict], cache) -> dict[str, torch.Tensor]:
+        """``{"behavior": (B, behavior_dim)}`` for windows keyed by (session_id,
+        bin_start), reusing the kv_proj rows of windows held in ``cache`` (a
+        ``cortex.cache.StreamingKVCache`` of (2 * latent_dim,) rows) and caching
+        those of the others. Same result as ``forward`` on the same events."""
+        from cortex.cache.kv_forward import forward_with_kv_cache
+
+        return {"behavior": forward_with_kv_cache(self, windows, cache)}
+
     def batch_runner(self):
         """The packed-batch runner host-index forwards go through (cortex.batching)."""
         if self._batch_runner is None:

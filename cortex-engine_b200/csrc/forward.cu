@@ -158,12 +158,26 @@ extern "C" size_t ck_forward_workspace_bytes(const ck_model* m, int64_t E, int32
 
 namespace {
 
+// Which part of the forward runs, split at the packed keys|values of the
+// events (the streaming K|V cache reuses those rows across calls).
+enum Stage { kFull = 0, kKvOnly = 1, kFromKv = 2 };
+
+struct KvIo {
+  Stage stage;
+  void* kv;          // kKvOnly: destination rows; kFromKv: source rows (else NULL)
+  int32_t* offsets;  // window offsets (B + 1), written / read like kv
+};
+
 // The forward over E events, of which events *n_valid..E-1 are padding when
-// n_valid (a device word) is given.
+// n_valid (a device word) is given. With io.stage == kFromKv, E is the number
+// of K|V rows in io.kv and no event arrays are read.
 int forward_impl(const ck_model* m, const void* nid, const void* tb, const void* val,
                  const void* bidx, int idx_dt, int64_t E, int32_t B, const int32_t* n_valid,
-                 void* out, void* ws, size_t ws_bytes, void* stream) {
-  if (m == nullptr || out == nullptr || B <= 0 || E < 0) return CK_ERR_INVALID_ARG;
+                 void* out, void* ws, size_t ws_bytes, void* stream,
+                 KvIo io = {kFull, nullptr, nullptr}) {
+  if (m == nullptr || B <= 0 || E < 0) return CK_ERR_INVALID_ARG;
+  if (io.stage != kKvOnly && out == nullptr) return CK_ERR_INVALID_ARG;
+  if (io.stage != kFull && (io.kv == nullptr || io.offsets == nullptr)) return CK_ERR_INVALID_ARG;
   if (m->dtype != CK_BF16 && m->dtype != CK_F32) return CK_ERR_UNSUPPORTED;
   if (m->latent_dim <= 0 || m->hidden_dim <= 0 || m->num_latents <= 0 || m->num_heads <= 0 ||
       m->cross_heads <= 0 || m->head_dim <= 0 || m->mlp_hidden <= 0 || m->behavior_dim <= 0 ||
@@ -172,14 +186,15 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
   if (m->num_heads * m->head_dim != m->latent_dim) return CK_ERR_INVALID_ARG;
   if (m->latent_dim % m->cross_heads != 0) return CK_ERR_INVALID_ARG;
   if (m->num_layers > 0 && m->blocks == nullptr) return CK_ERR_INVALID_ARG;
-  if (E > 0 && (!nid || !tb || !val || !bidx)) return CK_ERR_INVALID_ARG;
+  if (io.stage != kFromKv && E > 0 && (!nid || !tb || !val || !bidx)) return CK_ERR_INVALID_ARG;
   const Layout lay = plan(m, E, B);
   if (ws == nullptr || ws_bytes < lay.total + 256) return CK_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
   auto P = [&](size_t off) { return reinterpret_cast<void*>(base + off); };
   int32_t* counts = reinterpret_cast<int32_t*>(P(lay.counts));
-  int32_t* offsets = reinterpret_cast<int32_t*>(P(lay.offsets));
+  int32_t* offsets = io.offsets ? io.offsets : reinterpret_cast<int32_t*>(P(lay.offsets));
+  void* kv = io.kv ? io.kv : P(lay.kv);
   int32_t* dest = reinterpret_cast<int32_t*>(P(lay.dest));
   int32_t* emax = reinterpret_cast<int32_t*>(P(lay.emax));
   const int64_t D = m->latent_dim, Din = m->hidden_dim, L = m->num_latents;
@@ -194,23 +209,29 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     if (rc != CK_OK) return rc; \
   } while (0)
 
-  // 1. packing
-  CK_TRY(pack_events(bidx, idx_dt, 1, E, B, n_valid, counts, offsets, dest, emax, P(lay.packws),
-                     pack_workspace_bytes(E, B), st));
-  // 2. tokenizer + norm_kv, written in packed order
-  CK_TRY(tokenize(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din, m->n_vocab,
-                  m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1, 1, 1, E, dest,
-                  m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st, n_valid));
-  // 3. latent queries (batch-invariant)
-  CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
-                  CK_NORM_LAYER, P(lay.xq), D, st));
-  CK_TRY(lin(m, P(lay.xq), L, D, D, m->cross_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qc), D, st));
+  if (io.stage != kFromKv) {
+    // 1. packing
+    CK_TRY(pack_events(bidx, idx_dt, 1, E, B, n_valid, counts, offsets, dest, emax,
+                       P(lay.packws), pack_workspace_bytes(E, B), st));
+    // 2. tokenizer + norm_kv, written in packed order
+    CK_TRY(tokenize(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din, m->n_vocab,
+                    m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1, 1, 1, E, dest,
+                    m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st, n_valid));
+  }
   const bool fused_head = use_fused_head(m);
-  if (fused_head) CK_TRY(head_prep(m, P(lay.qall), st));
+  if (io.stage != kKvOnly) {
+    // 3. latent queries (batch-invariant)
+    CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
+                    CK_NORM_LAYER, P(lay.xq), D, st));
+    CK_TRY(lin(m, P(lay.xq), L, D, D, m->cross_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qc), D,
+               st));
+    if (fused_head) CK_TRY(head_prep(m, P(lay.qall), st));
+  }
   // 4. packed keys|values
-  if (E > 0)
-    CK_TRY(lin(m, P(lay.xkv), E, Din, Din, m->cross_kv, 2 * D, CK_EPI_STORE, nullptr, 0, 0,
-               P(lay.kv), 2 * D, st));
+  if (io.stage != kFromKv && E > 0)
+    CK_TRY(lin(m, P(lay.xkv), E, Din, Din, m->cross_kv, 2 * D, CK_EPI_STORE, nullptr, 0, 0, kv,
+               2 * D, st));
+  if (io.stage == kKvOnly) return CK_OK;
   // 5. cross attention over each sample's own events
   {
     const size_t es_b = m->dtype == CK_F32 ? 4 : 2;
@@ -224,11 +245,11 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     a.q_ld = D;
     a.q_rows = L;
     a.q_col_per_h = Dhc;
-    a.k = P(lay.kv);
+    a.k = kv;
     a.k_ld = 2 * D;
     a.k_rows = E > 0 ? E : 1;
     a.k_col_per_h = Dhc;
-    a.v = reinterpret_cast<uint8_t*>(P(lay.kv)) + D * es_b;
+    a.v = reinterpret_cast<uint8_t*>(kv) + D * es_b;
     a.v_ld = 2 * D;
     a.v_rows = E > 0 ? E : 1;
     a.v_col_per_h = Dhc;
@@ -373,6 +394,23 @@ extern "C" int ck_forward(const ck_model* m, const void* nid, const void* tb, co
                           const void* bidx, int idx_dt, int64_t E, int32_t B, void* out, void* ws,
                           size_t ws_bytes, void* stream) {
   return forward_impl(m, nid, tb, val, bidx, idx_dt, E, B, nullptr, out, ws, ws_bytes, stream);
+}
+
+extern "C" int ck_forward_kv(const ck_model* m, const int32_t* batch, int64_t capacity, int32_t B,
+                             void* kv, int32_t* offsets, void* ws, size_t ws_bytes, void* stream) {
+  if (batch == nullptr || capacity < 0 || capacity % 4 != 0) return CK_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(batch) & 15u) != 0) return CK_ERR_INVALID_ARG;
+  const int32_t* a = batch + CK_BATCH_HEADER_WORDS;
+  return forward_impl(m, a, a + capacity, a + 2 * capacity, a + 3 * capacity, CK_I32, capacity, B,
+                      batch, nullptr, ws, ws_bytes, stream, KvIo{kKvOnly, kv, offsets});
+}
+
+extern "C" int ck_forward_from_kv(const ck_model* m, const void* kv, int64_t n_rows,
+                                  const int32_t* offsets, int32_t B, void* out, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  return forward_impl(m, nullptr, nullptr, nullptr, nullptr, CK_I32, n_rows, B, nullptr, out, ws,
+                      ws_bytes, stream,
+                      KvIo{kFromKv, const_cast<void*>(kv), const_cast<int32_t*>(offsets)});
 }
 
 extern "C" int ck_forward_batch(const ck_model* m, const int32_t* batch, int64_t capacity,

@@ -111,6 +111,10 @@ int collate_bins(const ck_bin_window* wins, int32_t B, int32_t W, int32_t n_buck
                  int32_t max_neurons, int32_t* batch, int64_t capacity, void* ws, size_t ws_bytes,
                  int32_t* n_total, cudaStream_t st);
 
+// row-segment copies (rows.cu)
+int copy_rows(const void* src, int64_t src_rows, void* dst, int64_t dst_rows, int64_t row_bytes,
+              const int32_t* segments, int32_t n_segments, cudaStream_t st);
+
 // behaviour head in algebraic form (head.cu): head_prep builds the weight-only
 // (NT, D) matrix once per forward, head_fused runs both LayerNorms, the
 // projection against it, the per-head softmax and out_proj in one kernel.

@@ -276,6 +276,29 @@ int ck_batch_stage(const void* neuron_ids, const void* time_bins, const void* va
 int ck_forward_batch(const ck_model* m, const int32_t* batch, int64_t capacity, int32_t B,
                      void* behavior_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ── streaming K|V reuse ──────────────────────────────────────────────────
+ * ck_forward split at the packed keys|values of the events, so that kv_proj
+ * rows of windows seen before can come from a cache (the StreamingKVCache of
+ * cortex/cache/streaming.py:79-236, wired to kv_proj outputs).
+ *
+ * ck_forward_kv: packing, tokenizer + norm_kv and kv_proj of a packed event
+ * batch; writes kv (capacity, 2 * latent_dim) rows grouped by window (window b
+ * at rows offsets[b] .. offsets[b+1]-1) and offsets (B + 1, device int32).
+ * ck_forward_from_kv: the rest of the forward (latent queries, cross
+ * attention over each window's rows, the self-attention stack, the head) from
+ * n_rows such rows. Workspace: ck_forward_workspace_bytes(m, rows, B).
+ * ck_copy_rows: segments (device int32, n x 3: src_row, dst_row, rows) copied
+ * between two row buffers of src_rows / dst_rows rows of row_bytes (a
+ * multiple of 16) each; a segment outside its buffer records CK_ERR_INDEX and
+ * is skipped. */
+int ck_forward_kv(const ck_model* m, const int32_t* batch, int64_t capacity, int32_t B, void* kv,
+                  int32_t* offsets, void* workspace, size_t workspace_bytes, void* stream);
+int ck_forward_from_kv(const ck_model* m, const void* kv, int64_t n_rows, const int32_t* offsets,
+                       int32_t B, void* behavior_out, void* workspace, size_t workspace_bytes,
+                       void* stream);
+int ck_copy_rows(const void* src, int64_t src_rows, void* dst, int64_t dst_rows,
+                 int64_t row_bytes, const int32_t* segments, int32_t n_segments, void* stream);
+
 /* ── event ingest from bin-count matrices ─────────────────────────────────
  * events_from_bin_matrix + bucket_values + collate_events
  * (cortex/data/nlb.py:74-114, 249-280, 492-512) on the device: B windows of
