@@ -13,7 +13,10 @@ device, so one graph serves every batch of its bucket.
 
 The device batch buffer, the forward workspace and the graphs belong to one
 ``_Arena`` per (device, stream): graphs bake in those addresses, so an arena
-that has to grow drops its graphs and re-captures them on demand.
+that has to grow drops its graphs and re-captures them on demand. A graph also
+bakes in the kernel selection of its capture: the library's environment
+switches (CK_PDL, CK_HEAD_FUSED, CK_NORM_FOLD, CK_LN_FUSE) are read then, and
+``BatchRunner.invalidate()`` makes later batches capture afresh.
 """
 
 from __future__ import annotations

@@ -295,6 +295,20 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// test_wait with acquire at cluster scope: the phase may have been completed by
+// arrivals of other CTAs of the cluster, whose writes become visible here.
+__device__ __forceinline__ bool mbar_test_wait_cl(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait. Polls the barrier phase (test_wait: the thread is never parked,
 // so a phase completed by a tcgen05.commit is seen at once) until it completes,
 // the shared abort flag is raised by another thread, or ~kWaitCycles SM cycles
@@ -310,6 +324,55 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   for (uint32_t n = 1;; ++n) {
     if (mbar_test_wait(bar, parity)) return true;
     if ((n & 63u) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        set_status(CK_ERR_TIMEOUT, site, (int)parity);
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ── thread-block clusters (distributed shared memory) ─────────────────────────
+
+__device__ __forceinline__ uint32_t cl_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of `local` (an address in this CTA's smem) in CTA `rank`
+__device__ __forceinline__ uint32_t cl_map(const void* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  return remote;
+}
+
+__device__ __forceinline__ void cl_store_f2(uint32_t remote, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(remote), "f"(v.x), "f"(v.y)
+               : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's
+// earlier (distributed) shared-memory writes at cluster scope.
+__device__ __forceinline__ void cl_mbar_arrive(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
+               : "memory");
+}
+
+// All threads of all CTAs of the cluster (every thread must call it).
+__device__ __forceinline__ void cl_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// mbar_wait for a barrier that other CTAs of the cluster arrive on.
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag, int site) {
+  const long long t0 = clock64();
+  for (uint32_t n = 0;; ++n) {
+    if (mbar_test_wait_cl(bar, parity)) return true;
+    if ((n & 63u) == 63u) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (clock64() - t0 > kWaitCycles) {
         set_status(CK_ERR_TIMEOUT, site, (int)parity);
@@ -431,6 +494,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
       : "r"(taddr));
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 32-bit words per thread to / from TMEM columns taddr..taddr+15 of the
+// warp's lane quarter (32x32b shape), and the wait for this thread's stores.
+__device__ __forceinline__ void tmem_st16w(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16w(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tc_wait_store() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile.

@@ -142,6 +142,34 @@ int lin_folded(const void* A, int64_t M, int64_t K, const ck_norm_fold& f, int64
                  &fz);
 }
 
+// LayerNorm fused into the residual GEMM before it (gemm_tc FUSE_LN) is on by
+// default; CK_LN_FUSE=0 in the environment runs separate LayerNorm kernels.
+bool ln_fuse_enabled() {
+  const char* v = std::getenv("CK_LN_FUSE");
+  return v == nullptr || std::strcmp(v, "0") != 0;
+}
+
+// Residual linear Y = aux + A W^T whose output feeds a LayerNorm X = LN(Y).
+// With bf16 activations and N = 512 (the two 256-column halves of a row block
+// on a CTA pair) one GEMM writes both Y and X; otherwise a LayerNorm kernel
+// follows the GEMM.
+int lin_resid_ln(const ck_model* m, const void* A, int64_t M, int64_t K,
+                 const ck_linear_weight& w, int64_t N, const void* aux, int64_t ld_aux,
+                 int64_t mod, void* Y, const void* g, const void* b, void* X, cudaStream_t st) {
+  if (ln_fuse_enabled() && m->dtype == CK_BF16 && w.w != nullptr && w.bias == nullptr &&
+      (w.dtype == CK_BF16 || w.dtype == CK_I8) && N == 512 && g != nullptr && al16(g) &&
+      (b == nullptr || al16(b)) && al16(X) &&
+      gemm_tc_supported(M, K, K, w.dtype, CK_W_NK, N, K, A, w.w, N, Y, CK_EPI_RESID, aux,
+                        ld_aux)) {
+    GemmFusion fz = {nullptr, nullptr, 0, kLnEps, nullptr, nullptr, X, N, g, b};
+    return gemm_tc(A, M, K, K, w.w, w.dtype, CK_W_NK, N, K, w.scale, CK_EPI_RESID, aux, ld_aux,
+                   mod, Y, N, st, &fz);
+  }
+  const int rc = lin(m, A, M, K, K, w, N, CK_EPI_RESID, aux, ld_aux, mod, Y, N, st);
+  if (rc != CK_OK) return rc;
+  return row_norm(Y, m->dtype, M, (int32_t)N, N, g, b, kLnEps, CK_NORM_LAYER, X, N, st);
+}
+
 ck_attention_args attn_base(const ck_model* m) {
   ck_attention_args a;
   memset(&a, 0, sizeof(a));
@@ -278,13 +306,19 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
            fold_tc_ok(m, m->blocks[i].mlp0_fold, m->blocks[i].mlp0, BL, D, Hm, P(lay.lat),
                       CK_EPI_GELU, P(lay.hbuf));
   };
-  // 6. out_proj + broadcast latent residual
-  if (fold_qkv(0))
+  // 6. out_proj + broadcast latent residual (and block 0's norm_attn of it)
+  bool x_ready = false;  // lay.x already holds norm_attn(lat) for the next block
+  if (fold_qkv(0)) {
     CK_TRY(lin_stats(m, P(lay.att), BL, D, m->cross_out, D, m->latents, D, L, P(lay.lat), stats,
                      st));
-  else
+  } else if (m->num_layers > 0) {
+    CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, m->cross_out, D, m->latents, D, L, P(lay.lat),
+                        m->blocks[0].norm_attn_w, m->blocks[0].norm_attn_b, P(lay.x), st));
+    x_ready = true;
+  } else {
     CK_TRY(lin(m, P(lay.att), BL, D, D, m->cross_out, D, CK_EPI_RESID, m->latents, D, L,
                P(lay.lat), D, st));
+  }
   // 7. self-attention blocks
   const size_t es_b = m->dtype == CK_F32 ? 4 : 2;
   for (int i = 0; i < m->num_layers; ++i) {
@@ -292,11 +326,13 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     if (fold_qkv(i)) {
       CK_TRY(lin_folded(P(lay.lat), BL, D, w.qkv_fold, 3 * D, CK_EPI_STORE, stats, P(lay.qkv), st));
     } else {
-      CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b,
-                      kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
+      if (!x_ready)
+        CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b,
+                        kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
       CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
                  3 * D, st));
     }
+    x_ready = false;
     ck_attention_args a = attn_base(m);
     a.B = B;
     a.H = (int32_t)H;
@@ -328,18 +364,22 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
       CK_TRY(lin_stats(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat), stats, st));
       CK_TRY(lin_folded(P(lay.lat), BL, D, w.mlp0_fold, Hm, CK_EPI_GELU, stats, P(lay.hbuf), st));
     } else {
-      CK_TRY(lin(m, P(lay.att), BL, D, D, w.out, D, CK_EPI_RESID, P(lay.lat), D, 0, P(lay.lat), D,
-                 st));
-      CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_mlp_w, w.norm_mlp_b,
-                      kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
+      CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat),
+                          w.norm_mlp_w, w.norm_mlp_b, P(lay.x), st));
       CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, Hm, CK_EPI_GELU, nullptr, 0, 0, P(lay.hbuf), Hm,
                  st));
     }
-    if (fold_qkv(i + 1))
+    if (fold_qkv(i + 1)) {
       CK_TRY(lin_stats(m, P(lay.hbuf), BL, Hm, w.mlp2, D, P(lay.lat), D, 0, P(lay.lat), stats, st));
-    else
+    } else if (i + 1 < m->num_layers) {
+      CK_TRY(lin_resid_ln(m, P(lay.hbuf), BL, Hm, w.mlp2, D, P(lay.lat), D, 0, P(lay.lat),
+                          m->blocks[i + 1].norm_attn_w, m->blocks[i + 1].norm_attn_b, P(lay.x),
+                          st));
+      x_ready = true;
+    } else {
       CK_TRY(lin(m, P(lay.hbuf), BL, Hm, Hm, w.mlp2, D, CK_EPI_RESID, P(lay.lat), D, 0,
                  P(lay.lat), D, st));
+    }
   }
   // 8-9. final_norm, head norm and the behaviour head in one kernel
   if (fused_head) {

@@ -30,9 +30,14 @@ struct GemmArgs {
   float norm_eps;
   const float* fold_cs;
   const float* fold_bw;
+  // LayerNorm of the residual output (FUSE_LN): a second output
+  //   y2 = (y - mean) * rstd * ln_gamma + ln_beta   over each full row of y,
+  // where the row's two BN-column halves belong to the two CTAs of a cluster.
+  const __nv_bfloat16* ln_gamma;
+  const __nv_bfloat16* ln_beta;  // may be NULL
 };
 
-enum Fuse { FUSE_NONE = 0, FUSE_NORM = 1, FUSE_STATS = 2 };
+enum Fuse { FUSE_NONE = 0, FUSE_NORM = 1, FUSE_STATS = 2, FUSE_LN = 3 };
 
 __device__ __forceinline__ int64_t residual_row(const GemmArgs& p, int m) {
   return p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;

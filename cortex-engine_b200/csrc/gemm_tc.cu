@@ -23,6 +23,14 @@
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1. All mbarrier waits are bounded
 // (common.cuh); a timeout raises a CTA-wide abort flag and every role drains.
+//
+// FUSE_LN (residual epilogue, N == 2 * BN): the two column halves of a row
+// block go to the two CTAs of a cluster. The regular epilogue pass writes the
+// residual output Y, forms per-row (mean, M2) of its columns and leaves Y
+// (bf16) in the TMEM accumulator; the partials go to both CTAs' shared memory
+// (local store + DSMEM store, mbarrier arrivals local and remote). Once a
+// row's four partials are in, a second pass reads Y back from TMEM and writes
+// its LayerNorm Y2 (the next block's normalised input).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -49,6 +57,7 @@ struct GemmCfg {
   // weights, whose arithmetic per element is heavy enough that two warps per
   // scheduler cannot keep up with the tensor cores; two per quarter otherwise
   // (and always in int8 mode, whose converter warps need the registers)
+  static constexpr bool LN = FUSE == 3;  // gemm::FUSE_LN
   static constexpr int EPI_WARPS = (WMODE != W_I8_NK && EPI == CK_EPI_GELU) ? 16 : 8;
   static constexpr int EPI_GROUPS = EPI_WARPS / 4;  // column slices of a tile
   static constexpr int EPI_COLS = BN / EPI_GROUPS;  // columns per epilogue warp per tile
@@ -59,24 +68,29 @@ struct GemmCfg {
   // per epilogue warp: two 32-row x 32-column bf16 store boxes (64B-swizzled)
   static constexpr int STG_WARP = (EPI_WARPS == 8 ? 2 : 1) * STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = LN ? 512 : 256;
+  // FUSE_LN: per accumulator buffer, the (mean, M2) partials of the 4 column
+  // quarters (2 CTAs x 2 warp column slices) of every row
+  static constexpr int XCH_SMEM = LN ? 2 * 4 * BM * 8 : 0;
   // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
   // one buffer per TMEM accumulator, so the epilogue reads them at smem latency
   static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * EPI_COLS * 8 : 0;
-  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM;
+  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM - XCH_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
   static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
   static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + BAR_BYTES;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + XCH_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
 };
 
 template <int BN, int WMODE, int EPI, int FUSE>
 __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmY, const GemmArgs p) {
+                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmY2,
+                   const GemmArgs p) {
   using C = GemmCfg<BN, WMODE, FUSE, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -86,14 +100,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
   uint8_t* sB8 = sB + C::STAGES * C::B_BYTES;
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
   float2* sFold = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);  // [8][2][BN/2] (FUSE_NORM)
-  uint8_t* sBar = reinterpret_cast<uint8_t*>(sFold) + C::FOLD_SMEM;
+  float2* sXch = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(sFold) + C::FOLD_SMEM);
+  uint8_t* sBar = reinterpret_cast<uint8_t*>(sXch) + C::XCH_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
   uint64_t* conv = empty + C::STAGES;
   uint64_t* tfull = conv + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sready = drain + 1;  // FUSE_LN: row partials of both CTAs are in sXch[acc]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sready + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -111,6 +127,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       mbar_init(&tempty[a], C::EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
+    if (C::LN)
+      for (int a = 0; a < 2; ++a) mbar_init(&sready[a], 2 * C::EPI_WARPS * 32);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -127,9 +145,25 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // FUSE_LN: the partner CTA's barriers are initialised before any remote arrival
+  if (C::LN) cl_sync();
   const uint32_t tmem_base = *tmem_slot;
   grid_dep_wait();
-  grid_dep_launch();
+  // Dependent grids may launch at once; FUSE_LN signals them only when its
+  // epilogue is done (measured on B200: the early signal made the Cortex
+  // forward 1.5-2 % slower with the fused LayerNorm, 1 % faster without it).
+  if (!C::LN) grid_dep_launch();
+  // Tile -> (row block, column block). FUSE_LN pairs the two column blocks of a
+  // row block on the two CTAs of a cluster (consecutive tiles, even stride).
+  auto tile_mn = [&](int tile, int& mt, int& nt) {
+    if (C::LN) {
+      mt = tile >> 1;
+      nt = tile & 1;
+    } else {
+      mt = tile % p.num_m_tiles;
+      nt = tile / p.num_m_tiles;
+    }
+  };
 
   if (warp == 0) {
     // ── TMA producer ──
@@ -138,8 +172,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int mt = tile % p.num_m_tiles;
-        const int nt = tile / p.num_m_tiles;
+        int mt, nt;
+        tile_mn(tile, mt, nt);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 1)) break;
           mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
@@ -246,8 +280,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       for (int j = 0; j < FPL; ++j) wfold[j * 32 + lane] = fold_next[j];
     }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mt = tile % p.num_m_tiles;
-      const int nt = tile / p.num_m_tiles;
+      int mt, nt;
+      tile_mn(tile, mt, nt);
       float nmean = 0.f, nrstd = 0.f;  // folded LayerNorm of this row (FUSE_NORM)
       if (FUSE == gemm::FUSE_NORM) {
         gemm::combine_stats(p, srow, nmean, nrstd);
@@ -308,7 +342,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
         if (kAhead && c + 1 < NCH) {
           tmem_ld32(tbase + (uint32_t)((c + 1) * 32), nxt);
           fetch_res(c + 1, rnxt);
-        } else if (c + 1 == NCH) {
+        } else if (c + 1 == NCH && !C::LN) {  // (FUSE_LN reads the tile again below)
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
@@ -317,7 +351,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
           uint32_t packed[16];
           epilogue_math<EPI, FUSE>(p, m, n0, cur, nmean, nrstd, wfold + acc * COLS + c * 32,
                                    (kPrefetch && n0 + 32 <= p.N) ? rcur : nullptr, packed);
-          if (FUSE == gemm::FUSE_STATS) {
+          if (C::LN) tmem_st16w(tbase + (uint32_t)(c * 32), packed);  // Y, for the norm pass
+          if (FUSE == gemm::FUSE_STATS || C::LN) {
             // statistics of the values as stored (bf16), shifted by the
             // segment's first value so the sum of squares does not cancel
 #pragma unroll
@@ -375,9 +410,82 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
         p.stats_out[(int64_t)seg * p.M + m] =
             make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
       }
+      if constexpr (C::LN) {
+        // Row statistics: this warp's (mean, M2) over its COLS columns goes to
+        // its slot in both CTAs' shared memory (local store, DSMEM store), with
+        // one arrival on each CTA's barrier; the four slots of a row then hold
+        // both CTAs' column halves.
+        const float mu = st_s1 / (float)COLS;
+        const float2 part = make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
+        const uint32_t peer = cl_rank() ^ 1u;
+        float2* xb = sXch + acc * (4 * BM);
+        float2* mine = xb + ((peer ^ 1u) * 2 + half) * BM + row;
+        *mine = part;
+        cl_store_f2(cl_map(mine, peer), part);
+        mbar_arrive(&sready[acc]);
+        cl_mbar_arrive(cl_map(&sready[acc], peer));
+        if (!mbar_wait_cl(&sready[acc], acc_phase, abort_flag, 6)) break;
+        float2 q[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = xb[k * BM + row];
+        const float mean = 0.25f * ((q[0].x + q[1].x) + (q[2].x + q[3].x));
+        float m2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float d = q[k].x - mean;
+          m2 += q[k].y + (float)COLS * d * d;
+        }
+        const float rstd = 1.0f / sqrtf(m2 / (float)(4 * COLS) + p.norm_eps);
+        // LN(Y): Y comes back from TMEM, where the first pass left it as bf16
+        tc_wait_store();
+#pragma unroll 1
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t yk[16], normed[16];
+          tmem_ld16w(tbase + (uint32_t)(c * 32), yk);
+          tc_wait_ld();
+          if (c + 1 == NCH) {
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+          }
+          const int n0 = nbase + c * 32;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 g = __ldg(reinterpret_cast<const uint4*>(p.ln_gamma + n0) + q4);
+            const uint4 b = p.ln_beta != nullptr
+                                ? __ldg(reinterpret_cast<const uint4*>(p.ln_beta + n0) + q4)
+                                : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+            const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int i = 4 * q4 + j;
+              float y0 = (bf16_lo(yk[i]) - mean) * rstd;
+              float y1 = (bf16_hi(yk[i]) - mean) * rstd;
+              y0 = y0 * bf16_lo(gw[j]) + bf16_lo(bw[j]);
+              y1 = y1 * bf16_hi(gw[j]) + bf16_hi(bw[j]);
+              normed[i] = cvt_bf16x2(y0, y1);
+            }
+          }
+          // the two boxes keep alternating: free once at most one store is pending
+          uint8_t* box = stg + (c & 1) * STG_BOX;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(normed[4 * q], normed[4 * q + 1], normed[4 * q + 2], normed[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && m0 < p.M) {
+            tma_store_2d(&tmY2, box, n0, m0);
+            bulk_commit();
+          }
+        }
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (C::LN) grid_dep_launch();
     if (lane == 0) bulk_wait<0>();  // stores complete before the CTA exits
   } else if (WMODE == W_I8_NK) {
     // ── int8 -> bf16 converter (4 warps) ──
@@ -420,19 +528,43 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  // FUSE_LN: neither CTA leaves while its partner may still write its shared memory
+  if (C::LN) cl_sync();
 }
 
 template <int BN, int WMODE, int EPI, int FUSE>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
-                const GemmArgs& a, cudaStream_t st) {
+                const CUtensorMap& ty2, const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<BN, WMODE, FUSE, EPI>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
+  static_assert(!C::LN || C::EPI_GROUPS == 2, "FUSE_LN: four column quarters per row");
   auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
     return record_cuda_error();
   const int tiles = a.num_m_tiles * a.num_n_tiles;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  return launch_pdl(kern, dim3(grid), dim3(C::NUM_THREADS), C::SMEM_BYTES, st, ta, tb, ty, a);
+  if (!C::LN) {
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    return launch_pdl(kern, dim3(grid), dim3(C::NUM_THREADS), C::SMEM_BYTES, st, ta, tb, ty, ty2,
+                      a);
+  }
+  // clusters of two CTAs (the two column halves of a row block), an even grid
+  const int sms = num_sms() & ~1;
+  const int grid = tiles < sms ? tiles : sms;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(C::NUM_THREADS);
+  cfg.dynamicSmemBytes = (size_t)C::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return finish_launch(cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, ty2, a));
 }
 
 // Instantiated combinations: a folded LayerNorm feeds only bf16 (N, K) weights
@@ -440,28 +572,37 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 // epilogues.
 template <int BN, int WMODE>
 int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb,
-                 const CUtensorMap& ty, const GemmArgs& a, cudaStream_t st) {
+                 const CUtensorMap& ty0, const CUtensorMap& ty2, const GemmArgs& a,
+                 cudaStream_t st) {
+  using gemm::FUSE_LN;
   using gemm::FUSE_NONE;
   using gemm::FUSE_NORM;
   using gemm::FUSE_STATS;
+  // every instantiation takes the second output map; only FUSE_LN writes it
+  if (fuse == FUSE_LN) {
+    if constexpr (BN == 256) {
+      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_LN>(ta, tb, ty0, ty2, a, st);
+    }
+    return CK_ERR_UNSUPPORTED;
+  }
   if (fuse == FUSE_NORM) {
     if constexpr (WMODE == W_BF16_NK) {
-      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NORM>(ta, tb, ty, a, st);
-      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NORM>(ta, tb, ty, a, st);
+      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NORM>(ta, tb, ty0, ty2, a, st);
+      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NORM>(ta, tb, ty0, ty2, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
   if (fuse == FUSE_STATS) {
     if constexpr (WMODE != W_I8_NK) {
-      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty, a, st);
+      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty0, ty2, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
   switch (epi) {
-    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE>(ta, tb, ty, a, st);
-    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE>(ta, tb, ty, a, st);
-    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_NONE>(ta, tb, ty, a, st);
-    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS, FUSE_NONE>(ta, tb, ty, a, st);
+    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
+    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
+    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
+    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
   }
   return CK_ERR_INVALID_ARG;
 }
@@ -524,8 +665,22 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.norm_eps = 0.f;
   a.fold_cs = nullptr;
   a.fold_bw = nullptr;
+  a.ln_gamma = nullptr;
+  a.ln_beta = nullptr;
   int fuse = gemm::FUSE_NONE;
-  if (fz != nullptr && fz->stats_out != nullptr) {
+  if (fz != nullptr && fz->ln_out != nullptr) {
+    // LayerNorm of the residual output as a second output: whole rows of
+    // N = 2 * 256 columns, one row block per cluster of two CTAs
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (epi != CK_EPI_RESID || BN != 256 || N != 2 * BN || fz->ln_gamma == nullptr ||
+        !al16(fz->ln_gamma) || (fz->ln_beta != nullptr && !al16(fz->ln_beta)) ||
+        !al16(fz->ln_out) || (fz->ln_ld * 2) % 16 != 0)
+      return CK_ERR_UNSUPPORTED;
+    a.ln_gamma = reinterpret_cast<const __nv_bfloat16*>(fz->ln_gamma);
+    a.ln_beta = reinterpret_cast<const __nv_bfloat16*>(fz->ln_beta);
+    a.norm_eps = fz->eps;
+    fuse = gemm::FUSE_LN;
+  } else if (fz != nullptr && fz->stats_out != nullptr) {
     if (epi != CK_EPI_RESID) return CK_ERR_UNSUPPORTED;
     a.stats_out = reinterpret_cast<float2*>(fz->stats_out);
     fuse = gemm::FUSE_STATS;
@@ -545,11 +700,18 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     fuse = gemm::FUSE_NORM;
   }
 
-  CUtensorMap ta, tb, ty;
+  CUtensorMap ta, tb, ty, ty2;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
     return CK_ERR_INVALID_ARG;
   if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 32, 32, 64))
     return CK_ERR_INVALID_ARG;
+  if (fuse == gemm::FUSE_LN) {
+    if (!make_tmap_2d(&ty2, fz->ln_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, fz->ln_ld, 32,
+                      32, 64))
+      return CK_ERR_INVALID_ARG;
+  } else {
+    ty2 = ty;
+  }
   bool ok;
   if (w_dtype == CK_I8) {
     ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldw, BK, BN, 0);
@@ -561,13 +723,13 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   if (!ok) return CK_ERR_INVALID_ARG;
 
   if (BN == 256) {
-    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, fuse, ta, tb, ty, a, st);
-    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, fuse, ta, tb, ty, a, st);
-    return dispatch_epi<256, W_BF16_KN>(epi, fuse, ta, tb, ty, a, st);
+    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
+    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
+    return dispatch_epi<256, W_BF16_KN>(epi, fuse, ta, tb, ty, ty2, a, st);
   }
-  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, fuse, ta, tb, ty, a, st);
-  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, fuse, ta, tb, ty, a, st);
-  return dispatch_epi<128, W_BF16_KN>(epi, fuse, ta, tb, ty, a, st);
+  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
+  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
+  return dispatch_epi<128, W_BF16_KN>(epi, fuse, ta, tb, ty, ty2, a, st);
 }
 
 }  // namespace ck

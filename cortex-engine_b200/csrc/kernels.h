@@ -51,6 +51,8 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
 //   stats_in   LayerNorm folded into this GEMM: A is the raw residual, W is
 //              W * gamma, fold_cs[n] = sum_k W[n,k] * gamma[k] (as stored),
 //              fold_bw[n] = sum_k W[n,k] * beta[k]
+//   ln_out     residual epilogue also writes LayerNorm(Y) (gamma ln_gamma, beta
+//              ln_beta or none, eps) to ln_out (row stride ln_ld): bf16, N = 512
 struct GemmFusion {
   void* stats_out;
   const void* stats_in;
@@ -58,6 +60,10 @@ struct GemmFusion {
   float eps;
   const float* fold_cs;
   const float* fold_bw;
+  void* ln_out = nullptr;
+  int64_t ln_ld = 0;
+  const void* ln_gamma = nullptr;
+  const void* ln_beta = nullptr;
 };
 int gemm_tc_block_n(int64_t N);
 int gemm_tc_stats_width(int64_t N, int w_dtype);  // column width of one statistics segment

@@ -26,6 +26,16 @@ def _rel(y, ref):
     return float((y - ref).norm() / ref.norm())
 
 
+def _launches(fn):
+    """fn()'s result and the number of kernels the library launched for it."""
+    from cortex import _lib
+
+    c0 = _lib.load().ck_launch_count()
+    out = fn()
+    torch.cuda.synchronize()
+    return out, _lib.load().ck_launch_count() - c0
+
+
 def _model(name):
     from cortex.workloads import WORKLOADS, build_model
 
@@ -172,11 +182,12 @@ def test_fused_head_matches_composed_head(monkeypatch, name, latents, layers):
     model = build_model(wl, DEV)
     inp, _ = make_inputs(wl, seed=4, batch=6)
     cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    with torch.no_grad():
+    with torch.no_grad():  # device indices: the eager path reads the switch every call
         monkeypatch.setenv("CK_HEAD_FUSED", "1")
-        fused = model(*(inp[k] for k in cols))["behavior"]
+        fused, n_fused = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
         monkeypatch.setenv("CK_HEAD_FUSED", "0")
-        composed = model(*(inp[k] for k in cols))["behavior"]
+        composed, n_comp = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+    assert n_fused < n_comp  # two different code paths ran
     p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
            for k, v in model.state_dict().items()}
     ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
@@ -203,17 +214,56 @@ def test_norm_fold_matches_separate_norms(monkeypatch, name):
                 nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
     inp, _ = make_inputs(wl, seed=6, batch=8)
     cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    with torch.no_grad():
+    with torch.no_grad():  # device indices: the eager path reads the switch every call
         monkeypatch.setenv("CK_NORM_FOLD", "1")
-        folded = model(*(inp[k] for k in cols))["behavior"]
+        folded = model(*(inp[k].to(DEV) for k in cols))["behavior"]
         monkeypatch.setenv("CK_NORM_FOLD", "0")
-        separate = model(*(inp[k] for k in cols))["behavior"]
+        separate = model(*(inp[k].to(DEV) for k in cols))["behavior"]
     p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
            for k, v in model.state_dict().items()}
     ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
     assert torch.isfinite(folded).all()
     assert _rel(folded, separate) <= 1e-2, _rel(folded, separate)
     assert _rel(folded, ref) <= TOL["bfloat16"], _rel(folded, ref)
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
+def test_layernorm_fused_into_residual_gemm(monkeypatch, name):
+    """Each LayerNorm after a residual GEMM with D = 512 is the GEMM's second
+    output (a CTA pair per row block exchanging row statistics through
+    distributed shared memory), against separate LayerNorm kernels and the
+    oracle, with non-trivial gamma / beta. cfg2 runs it on INT8 weights; cfg3
+    (B=256, ragged) gives every CTA pair several row blocks."""
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    with torch.no_grad():
+        g = torch.Generator(device="cpu").manual_seed(8)
+        for blk in model.encoder.self_attn_blocks:
+            for nrm in (blk.norm_attn, blk.norm_mlp):
+                nrm.weight.copy_(1 + 0.2 * torch.randn(nrm.weight.shape, generator=g))
+                nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
+    inp, _ = make_inputs(wl, seed=9, batch=None if name == "cfg3" else 8)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        monkeypatch.setenv("CK_LN_FUSE", "1")
+        fused, n_fused = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+        again = model(*(inp[k].to(DEV) for k in cols))["behavior"]
+        monkeypatch.setenv("CK_LN_FUSE", "0")
+        separate, n_sep = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+    assert torch.isfinite(fused).all()
+    assert torch.equal(fused, again)  # deterministic
+    assert n_sep - n_fused == 2 * wl.config.num_layers  # every block LayerNorm fused
+    assert _rel(fused, separate) <= 1e-2, _rel(fused, separate)
+    n = 16 if name == "cfg3" else fused.shape[0]  # oracle on a subset (windows are independent)
+    from cortex.sharding import slice_events
+
+    sub = slice_events({k: inp[k].numpy() for k in cols},
+                       np.bincount(inp["batch_indices"].numpy()), 0, n)
+    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
+           for k, v in model.state_dict().items()}
+    ref = O.forward(p32, wl.config, *(torch.from_numpy(sub[k]) for k in cols)).float()
+    assert _rel(fused[:n], ref) <= TOL["bfloat16"], _rel(fused[:n], ref)
 
 
 def test_norm_fold_follows_inplace_parameter_updates(monkeypatch):
