@@ -42,6 +42,7 @@ SOURCES = [
     "batch.cpp",
     "ingest.cu",
     "rows.cu",
+    "runner.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -66,7 +67,9 @@ def _deps_mtime() -> float:
 
 
 # Host-only sources (.cpp) go to the host compiler directly.
-HOST_CFLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-I", INCLUDE, "-I", CSRC]
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+HOST_CFLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-I", INCLUDE, "-I", CSRC,
+               "-I", os.path.join(CUDA_HOME, "include")]
 
 
 def _compile(src: str, force: bool, extra: list[str]) -> str:

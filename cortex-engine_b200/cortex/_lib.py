@@ -126,6 +126,14 @@ _SIGS = {
     "ck_batch_stage": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _vp, _i64,
                               ctypes.POINTER(_i32)]),
     "ck_forward_batch": (_int, [ctypes.POINTER(Model), _vp, _i64, _i32, _vp, _vp, _sz, _vp]),
+    "ck_runner_create": (_int, [ctypes.POINTER(Model), _i32, ctypes.POINTER(_vp)]),
+    "ck_runner_destroy": (None, [_vp]),
+    "ck_runner_stage": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _i64, _i32, ctypes.POINTER(_i32)]),
+    "ck_runner_launch": (_int, [_vp, _vp, _vp]),
+    "ck_runner_launch_batch": (_int, [_vp, _vp, _i64, _i32, _vp, _vp]),
+    "ck_runner_invalidate": (_int, [_vp, ctypes.POINTER(Model)]),
+    "ck_runner_counters": (_int, [_vp, ctypes.POINTER(ctypes.c_longlong),
+                                  ctypes.POINTER(ctypes.c_longlong)]),
     "ck_forward_kv": (_int, [ctypes.POINTER(Model), _vp, _i64, _i32, _vp, _vp, _vp, _sz, _vp]),
     "ck_forward_from_kv": (_int, [ctypes.POINTER(Model), _vp, _i64, _vp, _i32, _vp, _vp, _sz,
                                   _vp]),

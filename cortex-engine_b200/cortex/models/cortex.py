@@ -33,6 +33,22 @@ from cortex.models.perceiver import PerceiverEncoder, _layer_norm, _linear
 from cortex.models.tokenizer import SpikeTokenizer
 
 
+# Counts module / parameter / buffer registrations in the process (torch's
+# global registration hooks): while it is unchanged, no submodule swap or
+# parameter assignment can have happened, and a cached weight description
+# skips its slot-by-slot identity check.
+_REGISTRATIONS = [0]
+
+
+def _registered(*_args) -> None:
+    _REGISTRATIONS[0] += 1
+
+
+torch.nn.modules.module.register_module_module_registration_hook(_registered)
+torch.nn.modules.module.register_module_parameter_registration_hook(_registered)
+torch.nn.modules.module.register_module_buffer_registration_hook(_registered)
+
+
 class BehaviorDecoder(nn.Module):
     """Decode behaviour from the latent array (cortex/models/cortex.py:15-53)."""
 
@@ -87,6 +103,7 @@ class CortexModel(nn.Module):
         self.masked_spike_head = MaskedSpikeHead(config) if config.use_masked_spike_head else None
         self._native_lock = threading.Lock()
         self._native_key = None
+        self._native_epoch = -1
         self._native = None
         self._workspace: dict[torch.device, torch.Tensor] = {}
         self._batch_runner = None
@@ -101,15 +118,15 @@ class CortexModel(nn.Module):
             sc = module.weight_scale
             if sc.dtype != torch.float32 or not sc.is_contiguous():
                 sc = sc.float().contiguous()
-            keep.append(sc)
+            keep.append(sc.detach())
             w = module.weight_int8.contiguous()
-            keep.append(w)
+            keep.append(w.detach())
             lw.w, lw.dtype, lw.scale = w.data_ptr(), L.CK_I8, sc.data_ptr()
             if module.bias is not None:
                 raise NotImplementedError("biased linears are not on the Cortex hot path")
         else:
             w = module.weight.contiguous()
-            keep.append(w)
+            keep.append(w.detach())
             lw.w, lw.dtype, lw.scale = w.data_ptr(), L.dtype_code(w.dtype), None
             if module.bias is not None:
                 raise NotImplementedError("biased linears are not on the Cortex hot path")
@@ -140,8 +157,13 @@ class CortexModel(nn.Module):
         return dicts, names, objs
 
     def _state_unchanged(self) -> bool:
+        if self._native_epoch == _REGISTRATIONS[0]:
+            return True  # no module, parameter or buffer registered anywhere since the check
         key = self._native_key
-        return key is not None and all(map(operator.is_, map(dict.get, key[0], key[1]), key[2]))
+        same = key is not None and all(map(operator.is_, map(dict.get, key[0], key[1]), key[2]))
+        if same:
+            self._native_epoch = _REGISTRATIONS[0]
+        return same
 
     def native_model(self) -> L.Model:
         """The ``ck_model`` description of this module's weights (cached).
@@ -165,7 +187,7 @@ class CortexModel(nn.Module):
                 if x.dtype != dt:
                     raise TypeError(f"parameter dtype {x.dtype} differs from the model dtype {dt}")
                 x = x.contiguous()
-                keep.append(x)
+                keep.append(x.detach())  # the storage itself, even if .data is reassigned
                 return x.data_ptr()
 
             m = L.Model()
@@ -212,6 +234,7 @@ class CortexModel(nn.Module):
                                                self._lw(head.out_proj, keep))
             self._native = (m, keep, folds)
             self._native_key = key
+            self._native_epoch = _REGISTRATIONS[0]
             return m
 
     # LayerNorm folds (ck_norm_fold_weights): norm_attn into qkv_proj and norm_mlp

@@ -276,6 +276,32 @@ int ck_batch_stage(const void* neuron_ids, const void* time_bins, const void* va
 int ck_forward_batch(const ck_model* m, const int32_t* batch, int64_t capacity, int32_t B,
                      void* behavior_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ── native serving runner ────────────────────────────────────────────────
+ * Owns, for one device: two pinned staging slots, the device batch buffer, the
+ * forward workspace and one CUDA graph of ck_forward_batch per (B, capacity)
+ * bucket (captured on the bucket's first batch). The one place where the
+ * library allocates: ck_runner_create / the first batches of a size allocate,
+ * ck_runner_destroy frees. All launches of one runner use one stream.
+ *   ck_runner_stage   host index arrays -> pinned packed batch (ck_batch_stage);
+ *                     B = batch_size if > 0, else max(batch_indices) + 1
+ *   ck_runner_launch  one host-to-device copy, the bucket's graph, and a device
+ *                     copy of the (B, behavior_dim) result to behavior_out
+ *   ck_runner_launch_batch  the same from a packed batch already on the device
+ *   ck_runner_invalidate    drop the graphs (and take m's weights if m != NULL)
+ * Replaces the per-batch tensor building and the eager forward of
+ * InferenceWorker._run_batch_sync (cortex/serve/worker.py:166-214). */
+typedef struct ck_runner ck_runner;
+int ck_runner_create(const ck_model* m, int32_t max_graphs, ck_runner** runner);
+void ck_runner_destroy(ck_runner* runner);
+int ck_runner_stage(ck_runner* runner, const void* neuron_ids, const void* time_bins,
+                    const void* values, const void* batch_indices, int idx_dtype, int64_t E,
+                    int32_t batch_size, int32_t* B);
+int ck_runner_launch(ck_runner* runner, void* behavior_out, void* stream);
+int ck_runner_launch_batch(ck_runner* runner, const int32_t* batch, int64_t capacity, int32_t B,
+                           void* behavior_out, void* stream);
+int ck_runner_invalidate(ck_runner* runner, const ck_model* m);
+int ck_runner_counters(ck_runner* runner, long long* captures, long long* replays);
+
 /* ── streaming K|V reuse ──────────────────────────────────────────────────
  * ck_forward split at the packed keys|values of the events, so that kv_proj
  * rows of windows seen before can come from a cache (the StreamingKVCache of
