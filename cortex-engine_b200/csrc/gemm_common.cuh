@@ -11,6 +11,10 @@ namespace gemm {
 struct GemmArgs {
   int M, N, K;
   int num_m_tiles, num_n_tiles, num_k_blocks;
+  // Tiles [split_from, num_tiles) of the persistent schedule are half tiles:
+  // the last round's full tiles split into their two BN/2-column halves, so
+  // that a short last wave keeps twice as many SMs busy for half as long.
+  int split_from, num_tiles;
   const __nv_bfloat16* aux;
   int64_t ld_aux;
   int64_t aux_row_mod;

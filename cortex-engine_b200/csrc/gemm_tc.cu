@@ -32,6 +32,9 @@
 // row's four partials are in, a second pass reads Y back from TMEM and writes
 // its LayerNorm Y2 (the next block's normalised input).
 #include <cuda.h>
+
+#include <cstdlib>
+#include <cstring>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -84,6 +87,7 @@ struct GemmCfg {
   static constexpr int SMEM_BYTES =
       1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + XCH_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
+  static constexpr uint32_t IDESC_HALF = idesc_bf16(BM, BN / 2, 0u);  // split tiles (NK only)
 };
 
 template <int BN, int WMODE, int EPI, int FUSE>
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int num_tiles = p.num_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -155,14 +159,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
   if (!C::LN) grid_dep_launch();
   // Tile -> (row block, column block). FUSE_LN pairs the two column blocks of a
   // row block on the two CTAs of a cluster (consecutive tiles, even stride).
-  auto tile_mn = [&](int tile, int& mt, int& nt) {
+  // part: -1 for a whole tile, 0 / 1 for the first / second BN/2 columns of a
+  // split tile (tiles from p.split_from on).
+  auto tile_mn = [&](int tile, int& mt, int& nt, int& part) {
+    part = -1;
     if (C::LN) {
       mt = tile >> 1;
       nt = tile & 1;
-    } else {
-      mt = tile % p.num_m_tiles;
-      nt = tile / p.num_m_tiles;
+      return;
     }
+    if (tile >= p.split_from) {
+      part = (tile - p.split_from) & 1;
+      tile = p.split_from + ((tile - p.split_from) >> 1);
+    }
+    mt = tile % p.num_m_tiles;
+    nt = tile / p.num_m_tiles;
   };
 
   if (warp == 0) {
@@ -172,14 +183,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        int mt, nt;
-        tile_mn(tile, mt, nt);
+        int mt, nt, part;
+        tile_mn(tile, mt, nt, part);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 1)) break;
           mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
           if (WMODE == W_BF16_NK) {
-            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+            // (a split tile's second half starts BN/2 rows further; the box
+            // stays BN rows, of which its N = BN/2 MMA reads the first half)
+            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK,
+                        nt * BN + (part > 0 ? BN / 2 : 0));
           } else if (WMODE == W_BF16_KN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
@@ -210,6 +224,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mt_, nt_, part;
+        tile_mn(tile, mt_, nt_, part);
+        const uint32_t idesc = part >= 0 ? C::IDESC_HALF : C::IDESC;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -228,7 +245,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
             const uint64_t bdesc = (WMODE == W_BF16_KN)
                                        ? sw128_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
                                        : sw128_desc(b_addr + k * 32, 16, 1024);
-            tc_mma_ss(d_tmem, adesc, bdesc, C::IDESC, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -280,8 +297,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       for (int j = 0; j < FPL; ++j) wfold[j * 32 + lane] = fold_next[j];
     }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int mt, nt;
-      tile_mn(tile, mt, nt);
+      int mt, nt, part;
+      tile_mn(tile, mt, nt, part);
       float nmean = 0.f, nrstd = 0.f;  // folded LayerNorm of this row (FUSE_NORM)
       if (FUSE == gemm::FUSE_NORM) {
         gemm::combine_stats(p, srow, nmean, nrstd);
@@ -298,8 +315,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       const int m = mt * BM + row;
       float st_shift = 0.f, st_s1 = 0.f, st_s2 = 0.f;  // segment statistics (FUSE_STATS)
       int st_cnt = 0;
-      const int col0 = half * COLS;
-      const int nbase = nt * BN + col0;
+      // a split tile's BN/2 columns are spread over all column slices
+      const int col0 = part >= 0 ? half * (COLS / 2) : half * COLS;
+      const int nch = part >= 0 ? NCH / 2 : NCH;
+      const int nbase = nt * BN + (part > 0 ? BN / 2 : 0) + col0;
       const uint32_t tbase =
           tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + col0);
       const bool row_ok = m < p.M;
@@ -331,6 +350,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       tc_wait_ld();
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
+        if (c >= nch) break;
         float* cur = (kAhead && (c & 1)) ? vb : va;
         float* nxt = (c & 1) ? va : vb;
         uint4* rcur = (c & 1) ? rb : ra;
@@ -339,10 +359,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
           tmem_ld32(tbase + (uint32_t)(c * 32), va);
           tc_wait_ld();
         }
-        if (kAhead && c + 1 < NCH) {
+        if (kAhead && c + 1 < nch) {
           tmem_ld32(tbase + (uint32_t)((c + 1) * 32), nxt);
           fetch_res(c + 1, rnxt);
-        } else if (c + 1 == NCH && !C::LN) {  // (FUSE_LN reads the tile again below)
+        } else if (c + 1 == nch && !C::LN) {  // (FUSE_LN reads the tile again below)
           tc_fence_before();
           mbar_arrive(&tempty[acc]);
         }
@@ -398,7 +418,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
             bulk_commit();
           }
         }
-        if (kAhead && c + 1 < NCH) tc_wait_ld();
+        if (kAhead && c + 1 < nch) tc_wait_ld();
       }
       if (FUSE == gemm::FUSE_NORM && tile + (int)gridDim.x < num_tiles) {
 #pragma unroll
@@ -541,7 +561,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
     return record_cuda_error();
-  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int tiles = a.num_tiles;
   if (!C::LN) {
     const int grid = tiles < num_sms() ? tiles : num_sms();
     return launch_pdl(kern, dim3(grid), dim3(C::NUM_THREADS), C::SMEM_BYTES, st, ta, tb, ty, ty2,
@@ -631,6 +651,11 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
   return true;
 }
 
+bool gemm_split_enabled() {
+  const char* v = std::getenv("CK_GEMM_SPLIT");
+  return v == nullptr || std::strcmp(v, "0") != 0;
+}
+
 int gemm_tc_block_n(int64_t N) { return (N % 256 == 0 || N > 256) ? 256 : 128; }
 
 int gemm_tc_stats_width(int64_t N, int w_dtype) {
@@ -651,6 +676,8 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.num_m_tiles = (int)((M + BM - 1) / BM);
   a.num_n_tiles = (int)((N + BN - 1) / BN);
   a.num_k_blocks = (int)((K + BK - 1) / BK);
+  a.num_tiles = a.num_m_tiles * a.num_n_tiles;
+  a.split_from = a.num_tiles;
   a.aux = reinterpret_cast<const __nv_bfloat16*>(aux);
   a.ld_aux = ld_aux;
   a.aux_row_mod = aux_row_mod;
@@ -700,6 +727,17 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     fuse = gemm::FUSE_NORM;
   }
 
+  // Split the last round's tiles in two when that keeps the round to one wave
+  // (bf16 (N, K) weights without epilogue fusions; CK_GEMM_SPLIT=0 disables).
+  if (fuse == gemm::FUSE_NONE && w_dtype == CK_BF16 && w_layout == CK_W_NK && BN == 256 &&
+      (int64_t)a.num_n_tiles * BN == N && gemm_split_enabled()) {
+    const int sms = num_sms();
+    const int rem = a.num_tiles > sms ? a.num_tiles % sms : 0;
+    if (rem > 0 && 2 * rem <= sms) {
+      a.split_from = a.num_tiles - rem;
+      a.num_tiles += rem;
+    }
+  }
   CUtensorMap ta, tb, ty, ty2;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
     return CK_ERR_INVALID_ARG;

@@ -266,6 +266,26 @@ def test_gelu_epilogue_matches_torch_erf_gelu():
     assert (diff > 0).float().mean().item() < 1e-3
 
 
+@pytest.mark.parametrize("M,N,epi", [(8192, 2048, "gelu"), (8192, 2048, "store"),
+                                     (16384, 1024, "store"), (10000, 2048, "gelu")])
+def test_split_last_round_is_bit_identical(monkeypatch, M, N, epi):
+    """A persistent schedule whose last round is short runs that round as half
+    tiles (BN/2 columns, N=128 MMAs): bit-identical to whole tiles."""
+    from cortex import _lib as L
+    from cortex.kernels import _ops
+
+    torch.manual_seed(M + N)
+    x = torch.randn(M, 512, dtype=torch.bfloat16).to(DEV)
+    w = (torch.randn(N, 512) / math.sqrt(512)).to(torch.bfloat16).to(DEV)
+    e = L.CK_EPI_GELU if epi == "gelu" else L.CK_EPI_STORE
+    monkeypatch.setenv("CK_GEMM_SPLIT", "1")
+    split = _ops.linear(x, w, epi=e)
+    monkeypatch.setenv("CK_GEMM_SPLIT", "0")
+    whole = _ops.linear(x, w, epi=e)
+    assert torch.equal(split, whole)
+    _status_ok()
+
+
 @pytest.mark.parametrize("epi", ["gelu", "resid", "resid_mod", "bias"])
 def test_linear_epilogues(epi):
     from cortex import _lib as L
