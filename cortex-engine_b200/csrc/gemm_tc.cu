@@ -54,8 +54,12 @@ constexpr int STG_BOX = 32 * 32 * 2;  // one 32-row x 32-col bf16 store box (64B
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
-template <int BN, int WMODE, int FUSE = 0, int EPI = CK_EPI_STORE>
+template <int BN, int WMODE, int FUSE = 0, int EPI = CK_EPI_STORE, bool PAIR_ = false>
 struct GemmCfg {
+  // PAIR: 2-SM MMA. A cluster of two CTAs computes a 256-row tile: each CTA
+  // holds its 128 rows of A and of the accumulator and half of B's BN rows;
+  // the even CTA issues the cta_group::2 MMAs for both.
+  static constexpr bool PAIR = PAIR_;
   // epilogue warps: four per TMEM lane quarter for the GELU epilogue with bf16
   // weights, whose arithmetic per element is heavy enough that two warps per
   // scheduler cannot keep up with the tensor cores; two per quarter otherwise
@@ -65,7 +69,7 @@ struct GemmCfg {
   static constexpr int EPI_GROUPS = EPI_WARPS / 4;  // column slices of a tile
   static constexpr int EPI_COLS = BN / EPI_GROUPS;  // columns per epilogue warp per tile
   static constexpr int A_BYTES = BM * BK * 2;                        // 16 KB
-  static constexpr int B_BYTES = BN * BK * 2;                        // bf16 operand
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;     // bf16 operand (this CTA's)
   static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
   // per epilogue warp: two 32-row x 32-column bf16 store boxes (64B-swizzled)
@@ -80,7 +84,8 @@ struct GemmCfg {
   static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * EPI_COLS * 8 : 0;
   static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM - XCH_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
-  static constexpr int TX_BYTES = A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES);
+  // bytes completing one stage's barrier (PAIR: both CTAs' loads, on the even CTA's)
+  static constexpr int TX_BYTES = (PAIR ? 2 : 1) * (A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES));
   static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
   static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
@@ -88,14 +93,16 @@ struct GemmCfg {
       1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + XCH_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
   static constexpr uint32_t IDESC_HALF = idesc_bf16(BM, BN / 2, 0u);  // split tiles (NK only)
+  static constexpr uint32_t IDESC_PAIR = idesc_bf16(2 * BM, BN, 0u);   // PAIR (NK only)
 };
 
-template <int BN, int WMODE, int EPI, int FUSE>
-__global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
+template <int BN, int WMODE, int EPI, int FUSE, bool PAIR = false>
+__global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmY2,
                    const GemmArgs p) {
-  using C = GemmCfg<BN, WMODE, FUSE, EPI>;
+  using C = GemmCfg<BN, WMODE, FUSE, EPI, PAIR>;
+  static_assert(!PAIR || (WMODE == W_BF16_NK && FUSE == 0), "PAIR: bf16 (N, K) weights, no fusion");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -128,7 +135,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], C::EPI_WARPS * 32);
+      // PAIR: the even CTA's copy collects both CTAs' epilogue threads
+      mbar_init(&tempty[a], (PAIR ? 2 : 1) * C::EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
     if (C::LN)
@@ -143,14 +151,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
     prefetch_tmap(&tmY);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // FUSE_LN: the partner CTA's barriers are initialised before any remote arrival
-  if (C::LN) cl_sync();
+  // FUSE_LN / PAIR: the partner CTA's barriers are initialised before any
+  // remote arrival or load completion
+  if (C::LN || PAIR) cl_sync();
+  const uint32_t crank = PAIR ? cl_rank() : 0u;  // PAIR: 0 issues the MMAs
+  // the tile loop of a PAIR cluster: both CTAs walk the same 256-row tiles
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const uint32_t tmem_base = *tmem_slot;
   grid_dep_wait();
   // Dependent grids may launch at once; FUSE_LN signals them only when its
@@ -172,8 +190,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       part = (tile - p.split_from) & 1;
       tile = p.split_from + ((tile - p.split_from) >> 1);
     }
-    mt = tile % p.num_m_tiles;
+    mt = tile % p.num_m_tiles;  // PAIR: 256-row tiles, this CTA's half
     nt = tile / p.num_m_tiles;
+    if (PAIR) mt = 2 * mt + (int)crank;
   };
 
   if (warp == 0) {
@@ -182,11 +201,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int tile = tile0; tile < num_tiles && !*abort_flag; tile += tstep) {
         int mt, nt, part;
         tile_mn(tile, mt, nt, part);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 1)) break;
+          if (PAIR) {
+            // both CTAs' bytes complete on the even CTA's barrier, which alone
+            // announces them
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
+            const uint32_t fb = cl_map(&full[stage], 0);
+            tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, fb, kb * BK, mt * BM);
+            tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, fb, kb * BK,
+                             nt * BN + (int)crank * (BN / 2));
+            ++issued;
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
           if (WMODE == W_BF16_NK) {
@@ -209,24 +243,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
           }
         }
       }
-      // Drain: make sure every issued copy has landed before the CTA can exit.
-      for (int s = 0; s < C::STAGES && s < issued; ++s) {
+      // Drain: make sure every issued copy has landed before the CTA can exit
+      // (PAIR: the even CTA's barriers count both CTAs' copies; the odd CTA is
+      // held by the cluster barrier before exit).
+      for (int s = 0; s < C::STAGES && s < issued && crank == 0; ++s) {
         const int last = issued - 1 - ((issued - 1 - s) % C::STAGES);
         mbar_wait(&full[s], (uint32_t)((last / C::STAGES) & 1), nullptr, 9);
       }
     }
   } else if (warp == 1) {
-    // ── MMA issuer ──
-    if (lane == 0) {
+    // ── MMA issuer (PAIR: the even CTA only) ──
+    if (lane == 0 && crank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = tile0; tile < num_tiles && ok; tile += tstep) {
         int mt_, nt_, part;
         tile_mn(tile, mt_, nt_, part);
-        const uint32_t idesc = part >= 0 ? C::IDESC_HALF : C::IDESC;
+        const uint32_t idesc = PAIR ? C::IDESC_PAIR : (part >= 0 ? C::IDESC_HALF : C::IDESC);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -245,21 +281,33 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
             const uint64_t bdesc = (WMODE == W_BF16_KN)
                                        ? sw128_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024)
                                        : sw128_desc(b_addr + k * 32, 16, 1024);
-            tc_mma_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (PAIR)
+              tc_mma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              tc_mma_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          if (PAIR)
+            tc_commit_pair(&empty[stage], 3);  // both CTAs' stage is free
+          else
+            tc_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if (PAIR)
+          tc_commit_pair(&tfull[acc], 3);  // both CTAs' accumulators are ready
+        else
+          tc_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
       // Drain all issued MMAs before TMEM / smem can be released.
-      tc_commit(drain);
+      if (PAIR)
+        tc_commit_pair(drain, 1);
+      else
+        tc_commit(drain);
       mbar_wait(drain, 0, nullptr, 8);
     }
   } else if (warp < C::CONV_WARP0) {
@@ -296,7 +344,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < FPL; ++j) wfold[j * 32 + lane] = fold_next[j];
     }
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int tile = tile0; tile < num_tiles; tile += tstep) {
       int mt, nt, part;
       tile_mn(tile, mt, nt, part);
       float nmean = 0.f, nrstd = 0.f;  // folded LayerNorm of this row (FUSE_NORM)
@@ -364,7 +412,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
           fetch_res(c + 1, rnxt);
         } else if (c + 1 == nch && !C::LN) {  // (FUSE_LN reads the tile again below)
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);
+          if (PAIR && crank != 0)
+            cl_mbar_arrive(cl_map(&tempty[acc], 0));  // the even CTA issues the MMAs
+          else
+            mbar_arrive(&tempty[acc]);
         }
         const int n0 = nbase + c * 32;
         if (n0 < p.N) {
@@ -513,7 +564,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int tile = tile0; tile < num_tiles && ok; tile += tstep) {
       for (int kb = 0; kb < p.num_k_blocks; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag, 5)) {
           ok = false;
@@ -544,32 +595,40 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI>::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // PAIR: the even CTA's MMAs (into both CTAs' TMEM, from both CTAs' shared
+  // memory) are drained before either CTA frees its columns or exits
+  if (PAIR) cl_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   // FUSE_LN: neither CTA leaves while its partner may still write its shared memory
   if (C::LN) cl_sync();
 }
 
-template <int BN, int WMODE, int EPI, int FUSE>
+template <int BN, int WMODE, int EPI, int FUSE, bool PAIR = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
                 const CUtensorMap& ty2, const GemmArgs& a, cudaStream_t st) {
-  using C = GemmCfg<BN, WMODE, FUSE, EPI>;
+  using C = GemmCfg<BN, WMODE, FUSE, EPI, PAIR>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
   static_assert(!C::LN || C::EPI_GROUPS == 2, "FUSE_LN: four column quarters per row");
-  auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE>;
+  auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE, PAIR>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
     return record_cuda_error();
   const int tiles = a.num_tiles;
-  if (!C::LN) {
+  if (!C::LN && !PAIR) {
     const int grid = tiles < num_sms() ? tiles : num_sms();
     return launch_pdl(kern, dim3(grid), dim3(C::NUM_THREADS), C::SMEM_BYTES, st, ta, tb, ty, ty2,
                       a);
   }
-  // clusters of two CTAs (the two column halves of a row block), an even grid
+  // clusters of two CTAs, an even grid: FUSE_LN, the two column halves of a
+  // row block (one tile each); PAIR, the two row halves of a 256-row tile (one
+  // tile per cluster)
   const int sms = num_sms() & ~1;
-  const int grid = tiles < sms ? tiles : sms;
+  const int grid = PAIR ? 2 * (tiles < sms / 2 ? tiles : sms / 2) : (tiles < sms ? tiles : sms);
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -590,6 +649,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 // Instantiated combinations: a folded LayerNorm feeds only bf16 (N, K) weights
 // with a store or GELU epilogue; statistics come only from bf16 residual
 // epilogues.
+// (dispatch value for a 2-SM pair launch, beside the gemm::Fuse modes)
+constexpr int FUSE_PAIR = 100;
+
 template <int BN, int WMODE>
 int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb,
                  const CUtensorMap& ty0, const CUtensorMap& ty2, const GemmArgs& a,
@@ -599,6 +661,13 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
   using gemm::FUSE_NORM;
   using gemm::FUSE_STATS;
   // every instantiation takes the second output map; only FUSE_LN writes it
+  if (fuse == FUSE_PAIR) {
+    if constexpr (BN == 256 && WMODE == W_BF16_NK) {
+      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE, true>(ta, tb, ty0, ty2, a, st);
+      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE, true>(ta, tb, ty0, ty2, a, st);
+    }
+    return CK_ERR_UNSUPPORTED;
+  }
   if (fuse == FUSE_LN) {
     if constexpr (BN == 256) {
       if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_LN>(ta, tb, ty0, ty2, a, st);
@@ -649,6 +718,16 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
     if (epi == CK_EPI_RESID && (ld_aux * 2) % 16 != 0) return false;
   }
   return true;
+}
+
+// 2-SM pairs by default only for long K: measured on B200 (bf16, 256-wide N
+// tiles) they take 8 % off 16384 x 2048 x 2048 and 2 % off 8192 x 2048 x 1024,
+// but nothing off K = 512 shapes, where the split last round is the better
+// tool. CK_GEMM_PAIR=1 / 0 forces them on / off.
+bool gemm_pair_enabled(int64_t K) {
+  const char* v = std::getenv("CK_GEMM_PAIR");
+  if (v != nullptr) return std::strcmp(v, "0") != 0;
+  return K >= 2048;
 }
 
 bool gemm_split_enabled() {
@@ -727,10 +806,21 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     fuse = gemm::FUSE_NORM;
   }
 
+  // 2-SM pairs (256-row tiles, B split over the pair): bf16 (N, K) weights, a
+  // store or GELU epilogue, no fusion, 256-wide N tiles, long K (see
+  // gemm_pair_enabled). The schedule then walks 256-row tiles.
+  bool pair = false;
+  if (fuse == gemm::FUSE_NONE && w_dtype == CK_BF16 && w_layout == CK_W_NK && BN == 256 &&
+      (epi == CK_EPI_STORE || epi == CK_EPI_GELU) && a.num_m_tiles >= 2 && gemm_pair_enabled(K)) {
+    pair = true;
+    a.num_m_tiles = (a.num_m_tiles + 1) / 2;
+    a.num_tiles = a.num_m_tiles * a.num_n_tiles;
+    a.split_from = a.num_tiles;
+  }
   // Split the last round's tiles in two when that keeps the round to one wave
   // (bf16 (N, K) weights without epilogue fusions; CK_GEMM_SPLIT=0 disables).
-  if (fuse == gemm::FUSE_NONE && w_dtype == CK_BF16 && w_layout == CK_W_NK && BN == 256 &&
-      (int64_t)a.num_n_tiles * BN == N && gemm_split_enabled()) {
+  if (!pair && fuse == gemm::FUSE_NONE && w_dtype == CK_BF16 && w_layout == CK_W_NK &&
+      BN == 256 && (int64_t)a.num_n_tiles * BN == N && gemm_split_enabled()) {
     const int sms = num_sms();
     const int rem = a.num_tiles > sms ? a.num_tiles % sms : 0;
     if (rem > 0 && 2 * rem <= sms) {
@@ -754,12 +844,14 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   if (w_dtype == CK_I8) {
     ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, ldw, BK, BN, 0);
   } else if (w_layout == CK_W_NK) {
-    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, ldw, BK, BN, 128);
+    ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, ldw, BK,
+                      pair ? BN / 2 : BN, 128);
   } else {
     ok = make_tmap_2d(&tb, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldw, 64, BK, 128);
   }
   if (!ok) return CK_ERR_INVALID_ARG;
 
+  if (pair) return dispatch_epi<256, W_BF16_NK>(epi, FUSE_PAIR, ta, tb, ty, ty2, a, st);
   if (BN == 256) {
     if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
     if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, a, st);

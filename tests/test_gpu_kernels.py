@@ -286,6 +286,32 @@ def test_split_last_round_is_bit_identical(monkeypatch, M, N, epi):
     _status_ok()
 
 
+@pytest.mark.parametrize("M,K,N,epi", [(8192, 512, 1536, "store"), (8192, 512, 2048, "gelu"),
+                                       (16384, 512, 1024, "store"), (300, 768, 2304, "store"),
+                                       (256, 512, 512, "gelu"), (1000, 2048, 512, "store")])
+def test_pair_mma_matches_single_cta(monkeypatch, M, K, N, epi):
+    """2-SM tiles (a CTA pair, 256 rows, B split over the pair, cta_group::2
+    MMAs issued by the even CTA) against one-CTA tiles and the fp32 product."""
+    from cortex import _lib as L
+    from cortex.kernels import _ops
+
+    torch.manual_seed(M + K + N)
+    x = torch.randn(M, K, dtype=torch.bfloat16)
+    w = (torch.randn(N, K) / math.sqrt(K)).to(torch.bfloat16)
+    e = L.CK_EPI_GELU if epi == "gelu" else L.CK_EPI_STORE
+    monkeypatch.setenv("CK_GEMM_PAIR", "1")
+    pair = _ops.linear(x.to(DEV), w.to(DEV), epi=e)
+    _status_ok()
+    monkeypatch.setenv("CK_GEMM_PAIR", "0")
+    single = _ops.linear(x.to(DEV), w.to(DEV), epi=e)
+    ref = _gemm_ref(x, w)
+    if epi == "gelu":
+        ref = torch.nn.functional.gelu(ref.to(torch.bfloat16).float())
+    rel = ((pair.float().cpu() - ref).norm() / ref.norm()).item()
+    assert rel < 5e-3, rel
+    assert torch.equal(pair, single)
+
+
 @pytest.mark.parametrize("epi", ["gelu", "resid", "resid_mod", "bias"])
 def test_linear_epilogues(epi):
     from cortex import _lib as L
