@@ -30,6 +30,7 @@ SOURCES = [
     "tokenizer.cu",
     "norm.cu",
     "gemm_tc.cu",
+    "gemm_chain.cu",
     "gemm_simt.cu",
     "attention_tc.cu",
     "attention_ws.cu",

@@ -16,7 +16,7 @@ of the model description they were captured with: when the description
 changes (weights moved, recast or replaced, modules swapped) the runner drops
 its graphs. They also bake in the kernel selection of their capture: the
 library's environment switches (CK_PDL, CK_HEAD_FUSED, CK_NORM_FOLD,
-CK_LN_FUSE) are read then, and ``BatchRunner.invalidate()`` makes later
+CK_LN_FUSE, CK_CHAIN) are read then, and ``BatchRunner.invalidate()`` makes later
 batches capture afresh.
 """
 

@@ -245,6 +245,7 @@ def test_layernorm_fused_into_residual_gemm(monkeypatch, name):
                 nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
     inp, _ = make_inputs(wl, seed=9, batch=None if name == "cfg3" else 8)
     cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    monkeypatch.setenv("CK_CHAIN", "0")  # one launch per linear: the GEMM's own LayerNorm
     with torch.no_grad():
         monkeypatch.setenv("CK_LN_FUSE", "1")
         fused, n_fused = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
@@ -264,6 +265,78 @@ def test_layernorm_fused_into_residual_gemm(monkeypatch, name):
            for k, v in model.state_dict().items()}
     ref = O.forward(p32, wl.config, *(torch.from_numpy(sub[k]) for k in cols)).float()
     assert _rel(fused[:n], ref) <= TOL["bfloat16"], _rel(fused[:n], ref)
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
+def test_chained_gemms_match_separate_launches(monkeypatch, name):
+    """The linears between two attentions (out_proj + LayerNorm, mlp.0, mlp.2 +
+    the next block's LayerNorm, the next qkv_proj) as one chained launch, with
+    row-block counters between the linears and the LayerNorm row statistics
+    exchanged inside a CTA pair, against one launch per linear and the oracle.
+    cfg2's block linears are all INT8, which chains do not take: it runs the
+    same launches either way. cfg3 (B=256, ragged events) gives every cluster
+    several jobs per linear."""
+    from cortex.sharding import slice_events
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    with torch.no_grad():
+        g = torch.Generator(device="cpu").manual_seed(12)
+        for blk in model.encoder.self_attn_blocks:
+            for nrm in (blk.norm_attn, blk.norm_mlp):
+                nrm.weight.copy_(1 + 0.2 * torch.randn(nrm.weight.shape, generator=g))
+                nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
+    inp, _ = make_inputs(wl, seed=13, batch=None if name == "cfg3" else 8)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():  # device indices: the eager path reads the switch every call
+        monkeypatch.setenv("CK_CHAIN", "1")
+        chained, n_chain = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+        again = model(*(inp[k].to(DEV) for k in cols))["behavior"]
+        monkeypatch.setenv("CK_CHAIN", "0")
+        separate, n_sep = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+    layers = wl.config.num_layers
+    assert torch.isfinite(chained).all()
+    assert torch.equal(chained, again)  # deterministic
+    # bf16: 2 + 4 L - 1 linears in L + 1 chains
+    assert n_sep - n_chain == (0 if wl.int8 else 3 * layers), (n_sep, n_chain)
+    if wl.int8:
+        assert torch.equal(chained, separate)
+    assert _rel(chained, separate) <= 1e-2, _rel(chained, separate)
+    n = 16 if name == "cfg3" else chained.shape[0]  # oracle on a subset (windows are independent)
+    sub = slice_events({k: inp[k].numpy() for k in cols},
+                       np.bincount(inp["batch_indices"].numpy()), 0, n)
+    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
+           for k, v in model.state_dict().items()}
+    ref = O.forward(p32, wl.config, *(torch.from_numpy(sub[k]) for k in cols)).float()
+    assert _rel(chained[:n], ref) <= TOL["bfloat16"], _rel(chained[:n], ref)
+
+
+@pytest.mark.parametrize("latents,batch", [(64, 3), (200, 5), (1000, 2)])
+def test_chained_gemms_ragged_row_blocks(monkeypatch, latents, batch):
+    """Chains whose row count B * L is not a multiple of the 128-row tile (the
+    last row block is partial: TMA clips its stores, its counters still count
+    every epilogue warp) and chains with fewer jobs than clusters."""
+    import dataclasses
+
+    from cortex.workloads import WORKLOADS, build_model, make_inputs
+
+    wl = WORKLOADS["cfg1"]
+    wl = dataclasses.replace(wl, config=wl.config.model_copy(update={"num_latents": latents,
+                                                                     "num_layers": 2}))
+    model = build_model(wl, DEV)
+    inp, _ = make_inputs(wl, seed=14, batch=batch)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        monkeypatch.setenv("CK_CHAIN", "1")
+        chained, n_chain = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+        monkeypatch.setenv("CK_CHAIN", "0")
+        separate, n_sep = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
+    assert n_sep - n_chain == 6
+    assert _rel(chained, separate) <= 1e-2, _rel(chained, separate)
+    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
+           for k, v in model.state_dict().items()}
+    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
+    assert _rel(chained, ref) <= TOL["bfloat16"], _rel(chained, ref)
 
 
 def test_norm_fold_follows_inplace_parameter_updates(monkeypatch):
