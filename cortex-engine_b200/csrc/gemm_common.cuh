@@ -39,6 +39,9 @@ struct GemmArgs {
   // where the row's two BN-column halves belong to the two CTAs of a cluster.
   const __nv_bfloat16* ln_gamma;
   const __nv_bfloat16* ln_beta;  // may be NULL
+  // FUSE_LN: the residual tile comes in by TMA (the kernel's residual map)
+  // ahead of the accumulator, else by per-row loads
+  int res_tma;
 };
 
 enum Fuse { FUSE_NONE = 0, FUSE_NORM = 1, FUSE_STATS = 2, FUSE_LN = 3 };

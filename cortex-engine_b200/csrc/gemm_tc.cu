@@ -25,12 +25,16 @@
 // (common.cuh); a timeout raises a CTA-wide abort flag and every role drains.
 //
 // FUSE_LN (residual epilogue, N == 2 * BN): the two column halves of a row
-// block go to the two CTAs of a cluster. The regular epilogue pass writes the
-// residual output Y, forms per-row (mean, M2) of its columns and leaves Y
-// (bf16) in the TMEM accumulator; the partials go to both CTAs' shared memory
-// (local store + DSMEM store, mbarrier arrivals local and remote). Once a
-// row's four partials are in, a second pass reads Y back from TMEM and writes
-// its LayerNorm Y2 (the next block's normalised input).
+// block go to the two CTAs of a cluster. Each epilogue warp has one store box
+// per 32-column chunk of its slice; the tile's residual arrives in them by
+// TMA before the accumulator is ready. The regular epilogue pass writes the
+// residual output Y through the boxes (each lane replaces its row's residual
+// with Y), forms per-row (mean, M2) of its columns and leaves Y (bf16) in the
+// TMEM accumulator; the partials go to both CTAs' shared memory (local store +
+// DSMEM store, mbarrier arrivals local and remote). Once a row's four partials
+// are in, a second pass reads Y back from TMEM and writes its LayerNorm Y2
+// (the next block's normalised input), with gamma and beta staged in shared
+// memory.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -72,8 +76,10 @@ struct GemmCfg {
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;     // bf16 operand (this CTA's)
   static constexpr int B8_BYTES = (WMODE == W_I8_NK) ? BN * BK : 0;  // int8 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + B8_BYTES;
-  // per epilogue warp: two 32-row x 32-column bf16 store boxes (64B-swizzled)
-  static constexpr int STG_WARP = (EPI_WARPS == 8 ? 2 : 1) * STG_BOX;
+  // per epilogue warp: 32-row x 32-column bf16 store boxes (64B-swizzled): one
+  // per chunk of its columns for FUSE_LN (they take the residual tile first),
+  // else two (one with four warps per lane quarter)
+  static constexpr int STG_WARP = (LN ? (BN / 2) / 32 : (EPI_WARPS == 8 ? 2 : 1)) * STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
   static constexpr int BAR_BYTES = LN ? 512 : 256;
   // FUSE_LN: per accumulator buffer, the (mean, M2) partials of the 4 column
@@ -82,7 +88,10 @@ struct GemmCfg {
   // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
   // one buffer per TMEM accumulator, so the epilogue reads them at smem latency
   static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * EPI_COLS * 8 : 0;
-  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM - XCH_SMEM;
+  // FUSE_LN: each epilogue warp's gamma | beta columns (bf16), staged once
+  static constexpr int GB_SMEM = LN ? EPI_WARPS * 2 * EPI_COLS * 2 : 0;
+  static constexpr int BUDGET =
+      232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM - XCH_SMEM - GB_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   // bytes completing one stage's barrier (PAIR: both CTAs' loads, on the even CTA's)
   static constexpr int TX_BYTES = (PAIR ? 2 : 1) * (A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES));
@@ -90,7 +99,7 @@ struct GemmCfg {
   static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + XCH_SMEM + BAR_BYTES;
+      1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + XCH_SMEM + GB_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
   static constexpr uint32_t IDESC_HALF = idesc_bf16(BM, BN / 2, 0u);  // split tiles (NK only)
   static constexpr uint32_t IDESC_PAIR = idesc_bf16(2 * BM, BN, 0u);   // PAIR (NK only)
@@ -100,7 +109,7 @@ template <int BN, int WMODE, int EPI, int FUSE, bool PAIR = false>
 __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmY2,
-                   const GemmArgs p) {
+                   const __grid_constant__ CUtensorMap tmR, const GemmArgs p) {
   using C = GemmCfg<BN, WMODE, FUSE, EPI, PAIR>;
   static_assert(!PAIR || (WMODE == W_BF16_NK && FUSE == 0), "PAIR: bf16 (N, K) weights, no fusion");
   extern __shared__ uint8_t smem_raw[];
@@ -112,7 +121,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
   float2* sFold = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);  // [8][2][BN/2] (FUSE_NORM)
   float2* sXch = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(sFold) + C::FOLD_SMEM);
-  uint8_t* sBar = reinterpret_cast<uint8_t*>(sXch) + C::XCH_SMEM;
+  uint8_t* sGB = reinterpret_cast<uint8_t*>(sXch) + C::XCH_SMEM;  // [EPI_WARPS][gamma | beta]
+  uint8_t* sBar = sGB + C::GB_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
   uint64_t* conv = empty + C::STAGES;
@@ -120,7 +130,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* sready = drain + 1;  // FUSE_LN: row partials of both CTAs are in sXch[acc]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sready + 2);
+  uint64_t* rbar = sready + 2;   // FUSE_LN: [EPI_WARPS] a warp's residual boxes have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + (C::LN ? C::EPI_WARPS : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -139,8 +150,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
       mbar_init(&tempty[a], (PAIR ? 2 : 1) * C::EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
-    if (C::LN)
+    if (C::LN) {
       for (int a = 0; a < 2; ++a) mbar_init(&sready[a], 2 * C::EPI_WARPS * 32);
+      for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&rbar[w], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -149,6 +162,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmY);
+    if (C::LN) {
+      prefetch_tmap(&tmY2);
+      if (p.res_tma) prefetch_tmap(&tmR);
+    }
   }
   if (warp == 1) {
     if (PAIR) {
@@ -344,6 +361,43 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
 #pragma unroll
       for (int j = 0; j < FPL; ++j) wfold[j * 32 + lane] = fold_next[j];
     }
+    // FUSE_LN: this warp's gamma | beta columns into shared memory (a CTA
+    // keeps one column half: tiles alternate halves and the stride is even),
+    // and the residual tile of each row block by TMA into the warp's boxes,
+    // issued before the tile's accumulator is ready.
+    uint8_t* wgb = sGB + e * (2 * COLS * 2);
+    const bool res_box = C::LN && p.res_tma != 0;
+    uint32_t rph = 0;
+    bool res_pending = false;
+    auto prefetch_res = [&](int tile) {
+      int mt, nt, part;
+      tile_mn(tile, mt, nt, part);
+      if (lane == 0) {
+        bulk_wait_read<0>();  // the boxes' last stores have read them
+        const int m0 = mt * BM + quarter * 32;
+        const int row0 = p.aux_row_mod > 0 ? (int)((int64_t)m0 % p.aux_row_mod) : m0;
+        mbar_arrive_expect_tx(&rbar[e], C::STG_WARP);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+          tma_load_2d(stg + c * STG_BOX, &tmR, &rbar[e], nt * BN + half * COLS + c * 32, row0);
+      }
+      res_pending = true;
+    };
+    if constexpr (C::LN) {
+      if (tile0 < num_tiles) {
+        static_assert(2 * COLS * 2 == 32 * 16, "FUSE_LN: one 16-byte piece of gamma | beta per lane");
+        int mt, nt, part;
+        tile_mn(tile0, mt, nt, part);
+        const int n0 = nt * BN + half * COLS;
+        const int k = lane & 15;
+        const __nv_bfloat16* src = lane < 16 ? p.ln_gamma : p.ln_beta;
+        *reinterpret_cast<uint4*>(wgb + lane * 16) =
+            src != nullptr ? __ldg(reinterpret_cast<const uint4*>(src + n0) + k)
+                           : make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+        if (res_box) prefetch_res(tile0);
+      }
+    }
     for (int tile = tile0; tile < num_tiles; tile += tstep) {
       int mt, nt, part;
       tile_mn(tile, mt, nt, part);
@@ -358,6 +412,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         }
       }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
+      if (res_box) {
+        if (!mbar_wait(&rbar[e], rph, abort_flag, 10)) break;
+        rph ^= 1;
+        res_pending = false;
+      } else if (C::LN && lane == 0) {
+        bulk_wait_read<0>();  // every box is free for this tile's first pass
+      }
       __syncwarp();
       tc_fence_after();
       const int m = mt * BM + row;
@@ -383,7 +444,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
       // four warps the other warps hide the load, and the registers are short)
       constexpr bool kPrefetch = EPI == CK_EPI_RESID && WMODE != W_I8_NK && C::EPI_WARPS == 8;
       auto fetch_res = [&](int c, uint4* dst) {
-        if (kPrefetch && row_ok && nbase + c * 32 + 32 <= p.N) {
+        if (kPrefetch && !res_box && row_ok && nbase + c * 32 + 32 <= p.N) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             dst[q] = __ldg(reinterpret_cast<const uint4*>(rrow + nbase + c * 32) + q);
@@ -419,9 +480,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         }
         const int n0 = nbase + c * 32;
         if (n0 < p.N) {
+          if (res_box) {  // the residual chunk from its box (this lane's row)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              rcur[q] = *reinterpret_cast<const uint4*>(stg + c * STG_BOX + lane * 64 +
+                                                        ((q ^ ((lane >> 1) & 3)) << 4));
+          }
           uint32_t packed[16];
           epilogue_math<EPI, FUSE>(p, m, n0, cur, nmean, nrstd, wfold + acc * COLS + c * 32,
-                                   (kPrefetch && n0 + 32 <= p.N) ? rcur : nullptr, packed);
+                                   ((kPrefetch || res_box) && n0 + 32 <= p.N) ? rcur : nullptr,
+                                   packed);
           if (C::LN) tmem_st16w(tbase + (uint32_t)(c * 32), packed);  // Y, for the norm pass
           if (FUSE == gemm::FUSE_STATS || C::LN) {
             // statistics of the values as stored (bf16), shifted by the
@@ -450,11 +518,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           // 64B-swizzled 32 x 32 box, then one TMA store per chunk; the box was
           // last read by the store issued two chunks ago
           // the box is free once the store that last used it has read it
-          uint8_t* box = stg + (NBOX == 2 ? (c & 1) : 0) * STG_BOX;
+          // (FUSE_LN: one box per chunk, all free since the tile began)
+          uint8_t* box = stg + (NBOX == 2 ? (c & 1) : NBOX == 1 ? 0 : c) * STG_BOX;
           if (lane == 0) {
             if (NBOX == 2)
               bulk_wait_read<1>();
-            else
+            else if (NBOX == 1)
               bulk_wait_read<0>();
           }
           __syncwarp();
@@ -521,10 +590,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           const int n0 = nbase + c * 32;
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
-            const uint4 g = __ldg(reinterpret_cast<const uint4*>(p.ln_gamma + n0) + q4);
-            const uint4 b = p.ln_beta != nullptr
-                                ? __ldg(reinterpret_cast<const uint4*>(p.ln_beta + n0) + q4)
-                                : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 g = *reinterpret_cast<const uint4*>(wgb + (c * 32 + q4 * 8) * 2);
+            const uint4 b = *reinterpret_cast<const uint4*>(wgb + (COLS + c * 32 + q4 * 8) * 2);
             const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
             const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -537,9 +604,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
               normed[i] = cvt_bf16x2(y0, y1);
             }
           }
-          // the two boxes keep alternating: free once at most one store is pending
-          uint8_t* box = stg + (c & 1) * STG_BOX;
-          if (lane == 0) bulk_wait_read<1>();
+          // box c is free once the first pass's store of it has read it: of the
+          // stores after that one (its later chunks, this pass's earlier ones)
+          // NCH - 1 may still be pending
+          uint8_t* box = stg + c * STG_BOX;
+          if (lane == 0) bulk_wait_read<NCH - 1>();
           __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -555,7 +624,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
+      if (res_box && tile + tstep < num_tiles) prefetch_res(tile + tstep);
     }
+    // a residual load still in flight (abort paths) lands before the CTA exits
+    if (res_pending) mbar_wait(&rbar[e], rph, nullptr, 11);
     if (C::LN) grid_dep_launch();
     if (lane == 0) bulk_wait<0>();  // stores complete before the CTA exits
   } else if (WMODE == W_I8_NK) {
@@ -611,7 +683,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
 
 template <int BN, int WMODE, int EPI, int FUSE, bool PAIR = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
-                const CUtensorMap& ty2, const GemmArgs& a, cudaStream_t st) {
+                const CUtensorMap& ty2, const CUtensorMap& tr, const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<BN, WMODE, FUSE, EPI, PAIR>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
   static_assert(!C::LN || C::EPI_GROUPS == 2, "FUSE_LN: four column quarters per row");
@@ -622,7 +694,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   if (!C::LN && !PAIR) {
     const int grid = tiles < num_sms() ? tiles : num_sms();
     return launch_pdl(kern, dim3(grid), dim3(C::NUM_THREADS), C::SMEM_BYTES, st, ta, tb, ty, ty2,
-                      a);
+                      tr, a);
   }
   // clusters of two CTAs, an even grid: FUSE_LN, the two column halves of a
   // row block (one tile each); PAIR, the two row halves of a 256-row tile (one
@@ -643,7 +715,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return finish_launch(cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, ty2, a));
+  return finish_launch(cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, ty2, tr, a));
 }
 
 // Instantiated combinations: a folded LayerNorm feeds only bf16 (N, K) weights
@@ -654,8 +726,8 @@ constexpr int FUSE_PAIR = 100;
 
 template <int BN, int WMODE>
 int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb,
-                 const CUtensorMap& ty0, const CUtensorMap& ty2, const GemmArgs& a,
-                 cudaStream_t st) {
+                 const CUtensorMap& ty0, const CUtensorMap& ty2, const CUtensorMap& tr,
+                 const GemmArgs& a, cudaStream_t st) {
   using gemm::FUSE_LN;
   using gemm::FUSE_NONE;
   using gemm::FUSE_NORM;
@@ -663,35 +735,35 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
   // every instantiation takes the second output map; only FUSE_LN writes it
   if (fuse == FUSE_PAIR) {
     if constexpr (BN == 256 && WMODE == W_BF16_NK) {
-      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE, true>(ta, tb, ty0, ty2, a, st);
-      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE, true>(ta, tb, ty0, ty2, a, st);
+      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
+      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
   if (fuse == FUSE_LN) {
     if constexpr (BN == 256) {
-      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_LN>(ta, tb, ty0, ty2, a, st);
+      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_LN>(ta, tb, ty0, ty2, tr, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
   if (fuse == FUSE_NORM) {
     if constexpr (WMODE == W_BF16_NK) {
-      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NORM>(ta, tb, ty0, ty2, a, st);
-      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NORM>(ta, tb, ty0, ty2, a, st);
+      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NORM>(ta, tb, ty0, ty2, tr, a, st);
+      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NORM>(ta, tb, ty0, ty2, tr, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
   if (fuse == FUSE_STATS) {
     if constexpr (WMODE != W_I8_NK) {
-      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty0, ty2, a, st);
+      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty0, ty2, tr, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
   switch (epi) {
-    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
-    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
-    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
-    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS, FUSE_NONE>(ta, tb, ty0, ty2, a, st);
+    case CK_EPI_STORE: return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE>(ta, tb, ty0, ty2, tr, a, st);
+    case CK_EPI_GELU: return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE>(ta, tb, ty0, ty2, tr, a, st);
+    case CK_EPI_RESID: return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_NONE>(ta, tb, ty0, ty2, tr, a, st);
+    case CK_EPI_BIAS: return launch_gemm<BN, WMODE, CK_EPI_BIAS, FUSE_NONE>(ta, tb, ty0, ty2, tr, a, st);
   }
   return CK_ERR_INVALID_ARG;
 }
@@ -773,6 +845,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.fold_bw = nullptr;
   a.ln_gamma = nullptr;
   a.ln_beta = nullptr;
+  a.res_tma = 0;
   int fuse = gemm::FUSE_NONE;
   if (fz != nullptr && fz->ln_out != nullptr) {
     // LayerNorm of the residual output as a second output: whole rows of
@@ -783,6 +856,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
         !al16(fz->ln_out) || (fz->ln_ld * 2) % 16 != 0)
       return CK_ERR_UNSUPPORTED;
     a.ln_gamma = reinterpret_cast<const __nv_bfloat16*>(fz->ln_gamma);
+
     a.ln_beta = reinterpret_cast<const __nv_bfloat16*>(fz->ln_beta);
     a.norm_eps = fz->eps;
     fuse = gemm::FUSE_LN;
@@ -828,7 +902,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
       a.num_tiles += rem;
     }
   }
-  CUtensorMap ta, tb, ty, ty2;
+  CUtensorMap ta, tb, ty, ty2, tr;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
     return CK_ERR_INVALID_ARG;
   if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 32, 32, 64))
@@ -839,6 +913,17 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
       return CK_ERR_INVALID_ARG;
   } else {
     ty2 = ty;
+  }
+  // FUSE_LN residual tiles by TMA: 32-row boxes, contiguous unless a broadcast
+  // period cuts them
+  a.res_tma = fuse == gemm::FUSE_LN && (aux_row_mod <= 0 || aux_row_mod % 32 == 0) &&
+              (ld_aux * 2) % 16 == 0;
+  if (a.res_tma) {
+    if (!make_tmap_2d(&tr, aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N,
+                      aux_row_mod > 0 ? (uint64_t)aux_row_mod : (uint64_t)M, ld_aux, 32, 32, 64))
+      return CK_ERR_INVALID_ARG;
+  } else {
+    tr = ty;
   }
   bool ok;
   if (w_dtype == CK_I8) {
@@ -851,15 +936,15 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   }
   if (!ok) return CK_ERR_INVALID_ARG;
 
-  if (pair) return dispatch_epi<256, W_BF16_NK>(epi, FUSE_PAIR, ta, tb, ty, ty2, a, st);
+  if (pair) return dispatch_epi<256, W_BF16_NK>(epi, FUSE_PAIR, ta, tb, ty, ty2, tr, a, st);
   if (BN == 256) {
-    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
-    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
-    return dispatch_epi<256, W_BF16_KN>(epi, fuse, ta, tb, ty, ty2, a, st);
+    if (w_dtype == CK_I8) return dispatch_epi<256, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, tr, a, st);
+    if (w_layout == CK_W_NK) return dispatch_epi<256, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, tr, a, st);
+    return dispatch_epi<256, W_BF16_KN>(epi, fuse, ta, tb, ty, ty2, tr, a, st);
   }
-  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
-  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, a, st);
-  return dispatch_epi<128, W_BF16_KN>(epi, fuse, ta, tb, ty, ty2, a, st);
+  if (w_dtype == CK_I8) return dispatch_epi<128, W_I8_NK>(epi, fuse, ta, tb, ty, ty2, tr, a, st);
+  if (w_layout == CK_W_NK) return dispatch_epi<128, W_BF16_NK>(epi, fuse, ta, tb, ty, ty2, tr, a, st);
+  return dispatch_epi<128, W_BF16_KN>(epi, fuse, ta, tb, ty, ty2, tr, a, st);
 }
 
 }  // namespace ck
