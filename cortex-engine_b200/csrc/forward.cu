@@ -117,6 +117,42 @@ int lin(const ck_model* m, const void* A, int64_t M, int64_t K, int64_t lda,
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The batch-invariant prologue (LayerNorm of the latent parameter, the cross
+// attention's q_proj, the head's weight-only matrix) runs on a side stream
+// forked from the caller's stream at the start of the forward and joined
+// before the cross attention, so it overlaps packing, the tokenizer and
+// kv_proj instead of preceding them. One side stream and event pair per host
+// thread and device (a stream that joins a graph capture is captured with it).
+// CK_SIDE=0 in the environment runs the prologue on the caller's stream.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+SideStream* side_stream() {
+  const char* v = std::getenv("CK_SIDE");
+  if (v != nullptr && std::strcmp(v, "0") == 0) return nullptr;
+  constexpr int kMaxDev = 16;
+  thread_local SideStream cache[kMaxDev];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  SideStream& ss = cache[dev];
+  if (ss.s == nullptr) {
+    SideStream n;
+    if (cudaStreamCreateWithFlags(&n.s, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess) {
+      (void)cudaGetLastError();
+      if (n.s) cudaStreamDestroy(n.s);
+      if (n.fork) cudaEventDestroy(n.fork);
+      if (n.join) cudaEventDestroy(n.join);
+      return nullptr;
+    }
+    ss = n;
+  }
+  return &ss;
+}
+
 // Can this residual linear emit row statistics (bf16 weights, tensor-core GEMM)?
 bool resid_tc_ok(const ck_model* m, const ck_linear_weight& w, int64_t M, int64_t K, int64_t N,
                  const void* A, const void* aux, int64_t ld_aux, const void* Y) {
@@ -355,11 +391,34 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     if (rc != CK_OK) return rc; \
   } while (0)
 
+  cudaEvent_t join_ev = nullptr;  // the side stream's prologue is done
   // chained GEMM launches for the latent stack: their counters start at zero
   const bool chains = io.stage != kKvOnly && m->num_layers > 0 && m->dtype == CK_BF16 &&
                       gemm_chain_enabled() && !norm_fold_enabled();
   if (chains && cudaMemsetAsync(P(lay.chain), 0, lay.chain_bytes, st) != cudaSuccess)
     return record_cuda_error();
+
+  const bool fused_head = use_fused_head(m);
+  if (io.stage != kKvOnly) {
+    // 3. latent queries (batch-invariant), on the side stream when there is one
+    SideStream* side = side_stream();
+    cudaStream_t ps = st;
+    if (side != nullptr) {
+      if (cudaEventRecord(side->fork, st) != cudaSuccess ||
+          cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
+        return record_cuda_error();
+      ps = side->s;
+    }
+    CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
+                    CK_NORM_LAYER, P(lay.xq), D, ps));
+    CK_TRY(lin(m, P(lay.xq), L, D, D, m->cross_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qc), D,
+               ps));
+    if (fused_head) CK_TRY(head_prep(m, P(lay.qall), ps));
+    if (side != nullptr) {
+      if (cudaEventRecord(side->join, ps) != cudaSuccess) return record_cuda_error();
+      join_ev = side->join;
+    }
+  }
 
   if (io.stage != kFromKv) {
     // 1. packing
@@ -370,20 +429,14 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
                     m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1, 1, 1, E, dest,
                     m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st, n_valid));
   }
-  const bool fused_head = use_fused_head(m);
-  if (io.stage != kKvOnly) {
-    // 3. latent queries (batch-invariant)
-    CK_TRY(row_norm(m->latents, m->dtype, L, (int32_t)D, D, m->norm_q_w, m->norm_q_b, kLnEps,
-                    CK_NORM_LAYER, P(lay.xq), D, st));
-    CK_TRY(lin(m, P(lay.xq), L, D, D, m->cross_q, D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qc), D,
-               st));
-    if (fused_head) CK_TRY(head_prep(m, P(lay.qall), st));
-  }
   // 4. packed keys|values
   if (io.stage != kFromKv && E > 0)
     CK_TRY(lin(m, P(lay.xkv), E, Din, Din, m->cross_kv, 2 * D, CK_EPI_STORE, nullptr, 0, 0, kv,
                2 * D, st));
   if (io.stage == kKvOnly) return CK_OK;
+  // the prologue's results (and the side stream) join the caller's stream
+  if (join_ev != nullptr && cudaStreamWaitEvent(st, join_ev, 0) != cudaSuccess)
+    return record_cuda_error();
   // 5. cross attention over each sample's own events
   {
     const size_t es_b = m->dtype == CK_F32 ? 4 : 2;
