@@ -69,6 +69,7 @@ class BatchRunner:
         self.model = model
         self._arenas: dict[tuple[torch.device, int], _Arena] = {}
         self._lock = threading.Lock()
+        self._bdim = int(model.config.behavior_dim)
 
     @property
     def captures(self) -> int:
@@ -86,12 +87,12 @@ class BatchRunner:
             for a in self._arenas.values():
                 L.check(L.load().ck_runner_invalidate(a.handle, None), "ck_runner_invalidate")
 
-    def _arena(self, dev: torch.device, stream: int) -> _Arena:
-        """The arena of (dev, stream), holding the model's current description."""
+    def _arena(self, dev: torch.device, stream: int, m) -> _Arena:
+        """The arena of (dev, stream), holding the model's current description m."""
         model = self.model
-        m = model.native_model()
-        model._refresh_folds()
         native = model._native
+        if native[2]:
+            model._refresh_folds()
         a = self._arenas.get((dev, stream))
         if a is None:
             a = _Arena(dev, m)
@@ -114,13 +115,11 @@ class BatchRunner:
         if not all(x.is_contiguous() for x in idx):
             idx = tuple(x.contiguous() for x in idx)
         E = int(idx[0].shape[0])
-        model = self.model
-        w0 = model.tokenizer.neuron_emb.weight
-        dev = w0.device
         lib = L.load()
         with self._lock:
+            m, dev, wdt = self.model.native_info()
             stream = L.stream_of(dev)
-            a = self._arena(dev, stream)
+            a = self._arena(dev, stream, m)
             B = ctypes.c_int32(0)
             rc = lib.ck_runner_stage(a.handle, idx[0].data_ptr(), idx[1].data_ptr(),
                                      idx[2].data_ptr(), idx[3].data_ptr(),
@@ -128,7 +127,7 @@ class BatchRunner:
                                      int(batch_size) if batch_size is not None else 0,
                                      ctypes.byref(B))
             L.check(rc, "ck_runner_stage")
-            out = torch.empty(B.value, model.config.behavior_dim, dtype=w0.dtype, device=dev)
+            out = torch.empty(B.value, self._bdim, dtype=wdt, device=dev)
             L.check(lib.ck_runner_launch(a.handle, out.data_ptr(), stream), "ck_runner_launch")
             return out
 
@@ -136,17 +135,15 @@ class BatchRunner:
         """(B, behavior_dim) from a packed batch already on the model's device
         (e.g. written by ck_collate_bins): one device copy into the runner's
         buffer, then the graph of its bucket."""
-        model = self.model
-        w0 = model.tokenizer.neuron_emb.weight
-        dev = w0.device
+        m, dev, wdt = self.model.native_info()
         if (batch.device != dev or batch.dtype != torch.int32
                 or batch.numel() < L.batch_words(capacity)):
             raise ValueError("forward_batch: an int32 packed batch on the model's device")
         with self._lock:
+            m, dev, wdt = self.model.native_info()
             stream = L.stream_of(dev)
-            a = self._arena(dev, stream)
-            out = torch.empty(int(batch_size), model.config.behavior_dim, dtype=w0.dtype,
-                              device=dev)
+            a = self._arena(dev, stream, m)
+            out = torch.empty(int(batch_size), self._bdim, dtype=wdt, device=dev)
             L.check(L.load().ck_runner_launch_batch(a.handle, batch.data_ptr(), capacity,
                                                     int(batch_size), out.data_ptr(), stream),
                     "ck_runner_launch_batch")

@@ -232,10 +232,17 @@ class CortexModel(nn.Module):
             m.head_q, m.head_kv, m.head_out = (self._lw(head.q_proj, keep),
                                                self._lw(head.kv_proj, keep),
                                                self._lw(head.out_proj, keep))
-            self._native = (m, keep, folds)
+            self._native = (m, keep, folds, tok.neuron_emb.weight.device, dt)
             self._native_key = key
             self._native_epoch = _REGISTRATIONS[0]
             return m
+
+    def native_info(self) -> tuple:
+        """(native description, weight device, weight dtype), from the cache when
+        the module tree is unchanged."""
+        self.native_model()
+        n = self._native
+        return n[0], n[3], n[4]
 
     # LayerNorm folds (ck_norm_fold_weights): norm_attn into qkv_proj and norm_mlp
     # into mlp.0, for bf16 weights. The folded weight is derived data; it is
@@ -340,13 +347,14 @@ class CortexModel(nn.Module):
             raise ValueError(
                 f"shape mismatch: neuron_ids={neuron_ids.shape}, time_bins={time_bins.shape}, "
                 f"values={values.shape}, batch_indices={batch_indices.shape}")
-        dev = self.tokenizer.neuron_emb.weight.device
-        L.require_cuda(self.tokenizer.neuron_emb.weight, what="CortexModel.forward")
-        if not return_aux and all(x.device.type == "cpu" for x in
-                                  (neuron_ids, time_bins, values, batch_indices)):
-            # host indices: one packed int32 batch, one copy, one graph replay
+        if not return_aux and (neuron_ids.device.type == time_bins.device.type ==
+                               values.device.type == batch_indices.device.type == "cpu"):
+            # host indices: one packed int32 batch, one copy, one graph replay (the
+            # weights' device is checked by the cached native description)
             return {"behavior": self.batch_runner().forward_host(
                 neuron_ids, time_bins, values, batch_indices, batch_size)}
+        dev = self.tokenizer.neuron_emb.weight.device
+        L.require_cuda(self.tokenizer.neuron_emb.weight, what="CortexModel.forward")
         E = int(batch_indices.shape[0])
         if batch_size is None:
             batch_size = int(batch_indices.max().item()) + 1 if E > 0 else 1
