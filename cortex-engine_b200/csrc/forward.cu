@@ -202,6 +202,7 @@ int lin_resid_ln(const ck_model* m, const void* A, int64_t M, int64_t K,
                  int64_t mod, void* Y, const void* g, const void* b, void* X, cudaStream_t st) {
   if (ln_fuse_enabled() && m->dtype == CK_BF16 && w.w != nullptr && w.bias == nullptr &&
       (w.dtype == CK_BF16 || w.dtype == CK_I8) && N == 512 && g != nullptr && al16(g) &&
+      (mod <= 0 || mod % 32 == 0) &&
       (b == nullptr || al16(b)) && al16(X) &&
       gemm_tc_supported(M, K, K, w.dtype, CK_W_NK, N, K, A, w.w, N, Y, CK_EPI_RESID, aux,
                         ld_aux)) {

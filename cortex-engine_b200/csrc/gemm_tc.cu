@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     // and the residual tile of each row block by TMA into the warp's boxes,
     // issued before the tile's accumulator is ready.
     uint8_t* wgb = sGB + e * (2 * COLS * 2);
-    const bool res_box = C::LN && p.res_tma != 0;
+    constexpr bool res_box = C::LN;  // (the host only fuses residuals it can box)
     uint32_t rph = 0;
     bool res_pending = false;
     auto prefetch_res = [&](int tile) {
@@ -416,8 +416,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         if (!mbar_wait(&rbar[e], rph, abort_flag, 10)) break;
         rph ^= 1;
         res_pending = false;
-      } else if (C::LN && lane == 0) {
-        bulk_wait_read<0>();  // every box is free for this tile's first pass
       }
       __syncwarp();
       tc_fence_after();
@@ -442,7 +440,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
       uint4 ra[4], rb[4];
       // (only the bf16 mode with two warps per lane quarter prefetches: with
       // four warps the other warps hide the load, and the registers are short)
-      constexpr bool kPrefetch = EPI == CK_EPI_RESID && WMODE != W_I8_NK && C::EPI_WARPS == 8;
+      constexpr bool kPrefetch =
+          EPI == CK_EPI_RESID && WMODE != W_I8_NK && C::EPI_WARPS == 8 && !res_box;
       auto fetch_res = [&](int c, uint4* dst) {
         if (kPrefetch && !res_box && row_ok && nbase + c * 32 + 32 <= p.N) {
 #pragma unroll
@@ -518,7 +517,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           // 64B-swizzled 32 x 32 box, then one TMA store per chunk; the box was
           // last read by the store issued two chunks ago
           // the box is free once the store that last used it has read it
-          // (FUSE_LN: one box per chunk, all free since the tile began)
+          // (FUSE_LN: one box per chunk, all free since the tile began; the
+          // chunks' stores go out together after the last one)
           uint8_t* box = stg + (NBOX == 2 ? (c & 1) : NBOX == 1 ? 0 : c) * STG_BOX;
           if (lane == 0) {
             if (NBOX == 2)
@@ -526,16 +526,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
             else if (NBOX == 1)
               bulk_wait_read<0>();
           }
-          __syncwarp();
+          if (!C::LN) __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
                 make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && m0 < p.M) {
-            tma_store_2d(&tmY, box, n0, m0);
-            bulk_commit();
+          if (!C::LN) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && m0 < p.M) {
+              tma_store_2d(&tmY, box, n0, m0);
+              bulk_commit();
+            }
           }
         }
         if (kAhead && c + 1 < nch) tc_wait_ld();
@@ -551,6 +553,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
             make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
       }
       if constexpr (C::LN) {
+        // the first pass's boxes (Y) go out together
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && m0 < p.M) {
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) tma_store_2d(&tmY, stg + c * STG_BOX, nbase + c * 32, m0);
+          bulk_commit();
+        }
         // Row statistics: this warp's (mean, M2) over its COLS columns goes to
         // its slot in both CTAs' shared memory (local store, DSMEM store), with
         // one arrival on each CTA's barrier; the four slots of a row then hold
@@ -576,7 +586,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           m2 += q[k].y + (float)COLS * d * d;
         }
         const float rstd = 1.0f / sqrtf(m2 / (float)(4 * COLS) + p.norm_eps);
-        // LN(Y): Y comes back from TMEM, where the first pass left it as bf16
+        // LN(Y): Y comes back from TMEM, where the first pass left it as bf16;
+        // the boxes are reused once the first pass's stores have read them
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
         tc_wait_store();
 #pragma unroll 1
         for (int c = 0; c < NCH; ++c) {
@@ -604,22 +617,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
               normed[i] = cvt_bf16x2(y0, y1);
             }
           }
-          // box c is free once the first pass's store of it has read it: of the
-          // stores after that one (its later chunks, this pass's earlier ones)
-          // NCH - 1 may still be pending
+          // box c was read by the first pass's store (waited for above)
           uint8_t* box = stg + c * STG_BOX;
-          if (lane == 0) bulk_wait_read<NCH - 1>();
-          __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
                 make_uint4(normed[4 * q], normed[4 * q + 1], normed[4 * q + 2], normed[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && m0 < p.M) {
-            tma_store_2d(&tmY2, box, n0, m0);
-            bulk_commit();
-          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && m0 < p.M) {
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) tma_store_2d(&tmY2, stg + c * STG_BOX, nbase + c * 32, m0);
+          bulk_commit();
         }
       }
       acc ^= 1;
@@ -852,6 +862,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     // N = 2 * 256 columns, one row block per cluster of two CTAs
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     if (epi != CK_EPI_RESID || BN != 256 || N != 2 * BN || fz->ln_gamma == nullptr ||
+        (aux_row_mod > 0 && aux_row_mod % 32 != 0) ||  // residual boxes of 32 rows
         !al16(fz->ln_gamma) || (fz->ln_beta != nullptr && !al16(fz->ln_beta)) ||
         !al16(fz->ln_out) || (fz->ln_ld * 2) % 16 != 0)
       return CK_ERR_UNSUPPORTED;
@@ -914,10 +925,9 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   } else {
     ty2 = ty;
   }
-  // FUSE_LN residual tiles by TMA: 32-row boxes, contiguous unless a broadcast
-  // period cuts them
-  a.res_tma = fuse == gemm::FUSE_LN && (aux_row_mod <= 0 || aux_row_mod % 32 == 0) &&
-              (ld_aux * 2) % 16 == 0;
+  // FUSE_LN residual tiles by TMA: 32-row boxes (a broadcast period is a
+  // multiple of 32, checked above)
+  a.res_tma = fuse == gemm::FUSE_LN;
   if (a.res_tma) {
     if (!make_tmap_2d(&tr, aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N,
                       aux_row_mod > 0 ? (uint64_t)aux_row_mod : (uint64_t)M, ld_aux, 32, 32, 64))

@@ -331,7 +331,10 @@ def test_chained_gemms_ragged_row_blocks(monkeypatch, latents, batch):
         chained, n_chain = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
         monkeypatch.setenv("CK_CHAIN", "0")
         separate, n_sep = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
-    assert n_sep - n_chain == 6
+    # 2 + 4 L - 1 linears in L + 1 chains; with a latent count that is not a
+    # multiple of 32 the separate path also keeps the cross LayerNorm apart
+    # (its broadcast residual does not come in 32-row boxes)
+    assert n_sep - n_chain == 6 + (1 if latents % 32 else 0), (n_sep, n_chain)
     assert _rel(chained, separate) <= 1e-2, _rel(chained, separate)
     p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
            for k, v in model.state_dict().items()}
