@@ -129,11 +129,26 @@ struct SideStream {
   cudaEvent_t fork = nullptr, join = nullptr;
 };
 
+// A host thread's side streams, released when the thread exits (errors are
+// ignored: at process exit the runtime may already be gone).
+struct SideStreams {
+  static constexpr int kMaxDev = 16;
+  SideStream dev[kMaxDev];
+  ~SideStreams() {
+    for (SideStream& ss : dev) {
+      if (ss.s) cudaStreamDestroy(ss.s);
+      if (ss.fork) cudaEventDestroy(ss.fork);
+      if (ss.join) cudaEventDestroy(ss.join);
+    }
+  }
+};
+
 SideStream* side_stream() {
   const char* v = std::getenv("CK_SIDE");
   if (v != nullptr && std::strcmp(v, "0") == 0) return nullptr;
-  constexpr int kMaxDev = 16;
-  thread_local SideStream cache[kMaxDev];
+  constexpr int kMaxDev = SideStreams::kMaxDev;
+  thread_local SideStreams streams;
+  SideStream* cache = streams.dev;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
   SideStream& ss = cache[dev];

@@ -342,6 +342,42 @@ def test_chained_gemms_ragged_row_blocks(monkeypatch, latents, batch):
     assert _rel(chained, ref) <= TOL["bfloat16"], _rel(chained, ref)
 
 
+def test_side_stream_prologue_is_bit_identical_and_per_thread(monkeypatch):
+    """The weight-only prologue (norm_q, q_proj, the head matrix) runs on a
+    side stream forked from the caller's stream; that changes the schedule
+    only. The result equals the single-stream forward bit for bit, also from
+    short-lived host threads, each of which creates its own side stream and
+    releases it when the thread exits."""
+    import threading
+
+    from cortex.workloads import make_inputs
+
+    wl, model = _model("cfg1")
+    inp, _ = make_inputs(wl, seed=15, batch=8)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    dev_inp = [inp[k].to(DEV) for k in cols]
+    with torch.no_grad():  # device indices: the eager path reads the switch every call
+        monkeypatch.setenv("CK_SIDE", "0")
+        single = model(*dev_inp)["behavior"]
+        monkeypatch.setenv("CK_SIDE", "1")
+        forked = model(*dev_inp)["behavior"]
+        results = []
+
+        def run():
+            with torch.no_grad():
+                y = model(*dev_inp)["behavior"]
+                torch.cuda.current_stream().synchronize()
+                results.append(y)
+
+        for _ in range(3):
+            t = threading.Thread(target=run)
+            t.start()
+            t.join()
+    torch.cuda.synchronize()
+    assert torch.equal(forked, single)
+    assert len(results) == 3 and all(torch.equal(y, single) for y in results)
+
+
 def test_norm_fold_follows_inplace_parameter_updates(monkeypatch):
     """The folded weights are derived data: an in-place update of a norm or a
     linear weight (version counter) rebuilds them before the next forward."""
