@@ -69,7 +69,8 @@ struct GemmCfg {
   // scheduler cannot keep up with the tensor cores; two per quarter otherwise
   // (and always in int8 mode, whose converter warps need the registers)
   static constexpr bool LN = FUSE == 3;  // gemm::FUSE_LN
-  static constexpr int EPI_WARPS = (WMODE != W_I8_NK && EPI == CK_EPI_GELU) ? 16 : 8;
+  static constexpr int EPI_WARPS =
+      (WMODE != W_I8_NK && (EPI == CK_EPI_GELU || LN)) ? 16 : 8;
   static constexpr int EPI_GROUPS = EPI_WARPS / 4;  // column slices of a tile
   static constexpr int EPI_COLS = BN / EPI_GROUPS;  // columns per epilogue warp per tile
   static constexpr int A_BYTES = BM * BK * 2;                        // 16 KB
@@ -79,17 +80,19 @@ struct GemmCfg {
   // per epilogue warp: 32-row x 32-column bf16 store boxes (64B-swizzled): one
   // per chunk of its columns for FUSE_LN (they take the residual tile first),
   // else two (one with four warps per lane quarter)
-  static constexpr int STG_WARP = (LN ? (BN / 2) / 32 : (EPI_WARPS == 8 ? 2 : 1)) * STG_BOX;
+  static constexpr int STG_WARP = (LN ? EPI_COLS / 32 : (EPI_WARPS == 8 ? 2 : 1)) * STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
   static constexpr int BAR_BYTES = LN ? 512 : 256;
   // FUSE_LN: per accumulator buffer, the (mean, M2) partials of the 4 column
   // quarters (2 CTAs x 2 warp column slices) of every row
-  static constexpr int XCH_SMEM = LN ? 2 * 4 * BM * 8 : 0;
+  static constexpr int XCH_SMEM = LN ? 2 * (2 * EPI_GROUPS) * BM * 8 : 0;
   // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
   // one buffer per TMEM accumulator, so the epilogue reads them at smem latency
   static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * EPI_COLS * 8 : 0;
   // FUSE_LN: each epilogue warp's gamma | beta columns (bf16), staged once
-  static constexpr int GB_SMEM = LN ? EPI_WARPS * 2 * EPI_COLS * 2 : 0;
+  // (two warps per lane quarter only: with four, the pipeline ring needs the room
+  // and the norm pass reads them through the read-only cache)
+  static constexpr int GB_SMEM = (LN && EPI_WARPS == 8) ? EPI_WARPS * 2 * EPI_COLS * 2 : 0;
   static constexpr int BUDGET =
       232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM - XCH_SMEM - GB_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
@@ -385,16 +388,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     };
     if constexpr (C::LN) {
       if (tile0 < num_tiles) {
-        static_assert(2 * COLS * 2 == 32 * 16, "FUSE_LN: one 16-byte piece of gamma | beta per lane");
-        int mt, nt, part;
-        tile_mn(tile0, mt, nt, part);
-        const int n0 = nt * BN + half * COLS;
-        const int k = lane & 15;
-        const __nv_bfloat16* src = lane < 16 ? p.ln_gamma : p.ln_beta;
-        *reinterpret_cast<uint4*>(wgb + lane * 16) =
-            src != nullptr ? __ldg(reinterpret_cast<const uint4*>(src + n0) + k)
-                           : make_uint4(0u, 0u, 0u, 0u);
-        __syncwarp();
+        if constexpr (C::GB_SMEM > 0) {
+          static_assert(2 * COLS * 2 == 32 * 16, "FUSE_LN: one 16-byte piece of gamma | beta per lane");
+          int mt, nt, part;
+          tile_mn(tile0, mt, nt, part);
+          const int n0 = nt * BN + half * COLS;
+          const int k = lane & 15;
+          const __nv_bfloat16* src = lane < 16 ? p.ln_gamma : p.ln_beta;
+          *reinterpret_cast<uint4*>(wgb + lane * 16) =
+              src != nullptr ? __ldg(reinterpret_cast<const uint4*>(src + n0) + k)
+                             : make_uint4(0u, 0u, 0u, 0u);
+          __syncwarp();
+        }
         if (res_box) prefetch_res(tile0);
       }
     }
@@ -563,29 +568,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         }
         // Row statistics: this warp's (mean, M2) over its COLS columns goes to
         // its slot in both CTAs' shared memory (local store, DSMEM store), with
-        // one arrival on each CTA's barrier; the four slots of a row then hold
-        // both CTAs' column halves.
+        // one arrival on each CTA's barrier; the NP slots of a row then hold
+        // both CTAs' column slices.
+        constexpr int NP = 2 * C::EPI_GROUPS;
         const float mu = st_s1 / (float)COLS;
         const float2 part = make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
-        const uint32_t peer = cl_rank() ^ 1u;
-        float2* xb = sXch + acc * (4 * BM);
-        float2* mine = xb + ((peer ^ 1u) * 2 + half) * BM + row;
+        const uint32_t self = cl_rank();
+        const uint32_t peer = self ^ 1u;
+        float2* xb = sXch + acc * (NP * BM);
+        float2* mine = xb + ((int)self * C::EPI_GROUPS + half) * BM + row;
         *mine = part;
         cl_store_f2(cl_map(mine, peer), part);
         mbar_arrive(&sready[acc]);
         cl_mbar_arrive(cl_map(&sready[acc], peer));
         if (!mbar_wait_cl(&sready[acc], acc_phase, abort_flag, 6)) break;
-        float2 q[4];
+        float2 q[NP];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) q[k] = xb[k * BM + row];
-        const float mean = 0.25f * ((q[0].x + q[1].x) + (q[2].x + q[3].x));
+        for (int k = 0; k < NP; ++k) q[k] = xb[k * BM + row];
+        float msum = 0.f;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) msum += q[k].x;
+        const float mean = msum / (float)NP;
         float m2 = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < NP; ++k) {
           const float d = q[k].x - mean;
           m2 += q[k].y + (float)COLS * d * d;
         }
-        const float rstd = 1.0f / sqrtf(m2 / (float)(4 * COLS) + p.norm_eps);
+        const float rstd = 1.0f / sqrtf(m2 / (float)(NP * COLS) + p.norm_eps);
         // LN(Y): Y comes back from TMEM, where the first pass left it as bf16;
         // the boxes are reused once the first pass's stores have read them
         if (lane == 0) bulk_wait_read<0>();
@@ -603,8 +613,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           const int n0 = nbase + c * 32;
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
-            const uint4 g = *reinterpret_cast<const uint4*>(wgb + (c * 32 + q4 * 8) * 2);
-            const uint4 b = *reinterpret_cast<const uint4*>(wgb + (COLS + c * 32 + q4 * 8) * 2);
+            uint4 g, b;
+            if constexpr (C::GB_SMEM > 0) {
+              g = *reinterpret_cast<const uint4*>(wgb + (c * 32 + q4 * 8) * 2);
+              b = *reinterpret_cast<const uint4*>(wgb + (COLS + c * 32 + q4 * 8) * 2);
+            } else {
+              g = __ldg(reinterpret_cast<const uint4*>(p.ln_gamma + n0) + q4);
+              b = p.ln_beta != nullptr ? __ldg(reinterpret_cast<const uint4*>(p.ln_beta + n0) + q4)
+                                       : make_uint4(0u, 0u, 0u, 0u);
+            }
             const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
             const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -696,7 +713,8 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
                 const CUtensorMap& ty2, const CUtensorMap& tr, const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<BN, WMODE, FUSE, EPI, PAIR>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
-  static_assert(!C::LN || C::EPI_GROUPS == 2, "FUSE_LN: four column quarters per row");
+  static_assert(!C::LN || C::EPI_GROUPS == 2 || C::EPI_GROUPS == 4,
+                "FUSE_LN: two or four column slices per CTA");
   auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE, PAIR>;
   if (!smem_attr_ready(reinterpret_cast<const void*>(kern), C::SMEM_BYTES))
     return record_cuda_error();
