@@ -60,8 +60,12 @@ def test_pack_golden_cases(golden_kernels):
 
 
 @pytest.mark.parametrize("E,B,sort", [(16384, 32, True), (214_000, 256, True),
-                                      (50_000, 300, False), (1, 1, True), (4097, 7, False)])
+                                      (50_000, 300, False), (1, 1, True), (4097, 7, False),
+                                      (65_536, 1024, False), (70_000, 40, False),
+                                      (30_000, 1500, True), (100_000, 2000, False)])
 def test_pack_random(E, B, sort):
+    """Counts, offsets, e_max and dest equal the oracle for sorted and unsorted
+    batches, from one event to 214k events and up to 2000 windows."""
     g = torch.Generator().manual_seed(E)
     b = torch.randint(0, B, (E,), generator=g)
     b[0] = B - 1
