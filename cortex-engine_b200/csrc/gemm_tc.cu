@@ -66,7 +66,9 @@ struct GemmCfg {
   static constexpr bool PAIR = PAIR_;
   // epilogue warps: four per TMEM lane quarter for the GELU epilogue with bf16
   // weights, whose arithmetic per element is heavy enough that two warps per
-  // scheduler cannot keep up with the tensor cores; two per quarter otherwise
+  // scheduler cannot keep up with the tensor cores, and for the fused
+  // LayerNorm with bf16 weights, whose two-pass epilogue is latency-bound and
+  // lies on the critical path (one tile per CTA); two per quarter otherwise
   // (and always in int8 mode, whose converter warps need the registers)
   static constexpr bool LN = FUSE == 3;  // gemm::FUSE_LN
   static constexpr int EPI_WARPS =
