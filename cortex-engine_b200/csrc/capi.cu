@@ -13,7 +13,7 @@ namespace ck {
 int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
                     int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale,
                     int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
-                    int64_t ldy, cudaStream_t st) {
+                    int64_t ldy, cudaStream_t st, bool w_static) {
   if (M < 0 || N < 0 || K < 0) return CK_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return CK_OK;
   if (!A || !W || !Y) return CK_ERR_INVALID_ARG;
@@ -24,8 +24,10 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
   if (w_dtype == CK_I8 && (w_scale == nullptr || w_layout != CK_W_NK)) return CK_ERR_INVALID_ARG;
   if (dtype == CK_BF16 && gemm_tc_supported(M, K, lda, w_dtype, w_layout, N, ldw, A, W, ldy, Y,
                                             epi, aux, ld_aux)) {
+    GemmFusion fz = {nullptr, nullptr, 0, 0.f, nullptr, nullptr};
+    fz.w_static = w_static;
     return gemm_tc(A, M, K, lda, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux, ld_aux,
-                   aux_row_mod, Y, ldy, st);
+                   aux_row_mod, Y, ldy, st, w_static ? &fz : nullptr);
   }
   return gemm_simt(A, dtype, M, K, lda, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux, ld_aux,
                    aux_row_mod, Y, ldy, st);

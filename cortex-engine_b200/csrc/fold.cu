@@ -21,7 +21,8 @@ __global__ void __launch_bounds__(256) norm_fold_kernel(const __nv_bfloat16* W, 
                                                         __nv_bfloat16* w_out, float* colsum,
                                                         float* bias) {
   grid_dep_wait();
-  grid_dep_launch();
+  // no early signal: the kernel after this one may read the weights written
+  // here before its own dependency wait (the tcgen05 GEMM's weight prefetch)
   const int lane = threadIdx.x & 31;
   const int64_t n = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (n >= N) return;

@@ -24,7 +24,7 @@ namespace ck {
 int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
                     int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale,
                     int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
-                    int64_t ldy, cudaStream_t st);
+                    int64_t ldy, cudaStream_t st, bool w_static);
 int attention_dispatch(const ck_attention_args& a, cudaStream_t st);
 }  // namespace ck
 
@@ -111,8 +111,9 @@ int lin(const ck_model* m, const void* A, int64_t M, int64_t K, int64_t lda,
   if (w.bias != nullptr) return CK_ERR_UNSUPPORTED;  // every linear on this path is bias-free
   const int wd = w.dtype;
   if (wd != m->dtype && wd != CK_I8) return CK_ERR_UNSUPPORTED;
+  // (the model's weights: no kernel of the forward writes them)
   return linear_dispatch(A, m->dtype, M, K, lda, w.w, wd, CK_W_NK, N, K, w.scale, epi, aux,
-                         ld_aux, mod, Y, ldy, st);
+                         ld_aux, mod, Y, ldy, st, true);
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -190,6 +191,7 @@ int lin_stats(const ck_model* m, const void* A, int64_t M, int64_t K, const ck_l
               int64_t N, const void* aux, int64_t ld_aux, int64_t mod, void* Y, void* stats,
               cudaStream_t st) {
   GemmFusion fz = {stats, nullptr, 0, 0.f, nullptr, nullptr};
+  fz.w_static = true;
   return gemm_tc(A, M, K, K, w.w, w.dtype, CK_W_NK, N, K, w.scale, CK_EPI_RESID, aux, ld_aux, mod,
                  Y, N, st, &fz);
 }
@@ -197,6 +199,7 @@ int lin_stats(const ck_model* m, const void* A, int64_t M, int64_t K, const ck_l
 int lin_folded(const void* A, int64_t M, int64_t K, const ck_norm_fold& f, int64_t N, int epi,
                const void* stats, void* Y, cudaStream_t st) {
   GemmFusion fz = {nullptr, stats, gemm_tc_stats_width(K, CK_BF16), 1e-5f, f.colsum, f.bias};
+  fz.w_static = true;
   return gemm_tc(A, M, K, K, f.w, CK_BF16, CK_W_NK, N, K, nullptr, epi, nullptr, 0, 0, Y, N, st,
                  &fz);
 }
@@ -222,6 +225,7 @@ int lin_resid_ln(const ck_model* m, const void* A, int64_t M, int64_t K,
       gemm_tc_supported(M, K, K, w.dtype, CK_W_NK, N, K, A, w.w, N, Y, CK_EPI_RESID, aux,
                         ld_aux)) {
     GemmFusion fz = {nullptr, nullptr, 0, kLnEps, nullptr, nullptr, X, N, g, b};
+    fz.w_static = true;
     return gemm_tc(A, M, K, K, w.w, w.dtype, CK_W_NK, N, K, w.scale, CK_EPI_RESID, aux, ld_aux,
                    mod, Y, N, st, &fz);
   }

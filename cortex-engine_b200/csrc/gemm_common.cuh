@@ -42,6 +42,7 @@ struct GemmArgs {
   // FUSE_LN: the residual tile comes in by TMA (the kernel's residual map)
   // ahead of the accumulator, else by per-row loads
   int res_tma;
+  int pre_b;  // B (the weight) may be prefetched before the dependency wait
 };
 
 enum Fuse { FUSE_NONE = 0, FUSE_NORM = 1, FUSE_STATS = 2, FUSE_LN = 3 };

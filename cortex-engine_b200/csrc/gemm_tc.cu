@@ -192,11 +192,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const uint32_t tmem_base = *tmem_slot;
-  grid_dep_wait();
-  // Dependent grids may launch at once; FUSE_LN signals them only when its
-  // epilogue is done (measured on B200: the early signal made the Cortex
-  // forward 1.5-2 % slower with the fused LayerNorm, 1 % faster without it).
-  if (!C::LN) grid_dep_launch();
   // Tile -> (row block, column block). FUSE_LN pairs the two column blocks of a
   // row block on the two CTAs of a cluster (consecutive tiles, even stride).
   // part: -1 for a whole tile, 0 / 1 for the first / second BN/2 columns of a
@@ -216,6 +211,35 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     nt = tile / p.num_m_tiles;
     if (PAIR) mt = 2 * mt + (int)crank;
   };
+
+  // When the caller vouches that the weight (B) is not written by the kernel
+  // this one may overlap (p.pre_b: model weights inside the forward), the
+  // producer issues the first ring stages' B loads before the dependency wait
+  // (one-CTA tiles with bf16 weights); their A loads follow the wait. The
+  // weights' HBM latency then runs under the previous kernel's tail.
+  int pre_b = 0;
+  if (p.pre_b && !PAIR && WMODE != W_I8_NK && warp == 0 && lane == 0 && tile0 < num_tiles) {
+    int mt, nt, part;
+    tile_mn(tile0, mt, nt, part);
+    pre_b = p.num_k_blocks < C::STAGES ? p.num_k_blocks : C::STAGES;
+    for (int kb = 0; kb < pre_b; ++kb) {
+      mbar_arrive_expect_tx(&full[kb], C::TX_BYTES);
+      if (WMODE == W_BF16_NK) {
+        tma_load_2d(sB + kb * C::B_BYTES, &tmB, &full[kb], kb * BK,
+                    nt * BN + (part > 0 ? BN / 2 : 0));
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j)
+          tma_load_2d(sB + kb * C::B_BYTES + j * (64 * BK * 2), &tmB, &full[kb], nt * BN + j * 64,
+                      kb * BK);
+      }
+    }
+  }
+  grid_dep_wait();
+  // Dependent grids may launch at once; FUSE_LN signals them only when its
+  // epilogue is done (measured on B200: the early signal made the Cortex
+  // forward 1.5-2 % slower with the fused LayerNorm, 1 % faster without it).
+  if (!C::LN) grid_dep_launch();
 
   if (warp == 0) {
     // ── TMA producer ──
@@ -243,9 +267,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
             }
             continue;
           }
-          mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
+          const bool pre = tile == tile0 && kb < pre_b;  // B already in flight
+          if (!pre) mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
-          if (WMODE == W_BF16_NK) {
+          if (pre) {
+          } else if (WMODE == W_BF16_NK) {
             // (a split tile's second half starts BN/2 rows further; the box
             // stays BN rows, of which its N = BN/2 MMA reads the first half)
             tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK,
@@ -876,6 +902,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.ln_gamma = nullptr;
   a.ln_beta = nullptr;
   a.res_tma = 0;
+  a.pre_b = (fz != nullptr && fz->w_static) ? 1 : 0;
   int fuse = gemm::FUSE_NONE;
   if (fz != nullptr && fz->ln_out != nullptr) {
     // LayerNorm of the residual output as a second output: whole rows of

@@ -64,7 +64,19 @@ struct GemmFusion {
   int64_t ln_ld = 0;
   const void* ln_gamma = nullptr;
   const void* ln_beta = nullptr;
+  // the weight is not written by the kernel launched just before on the stream
+  // (model weights inside the forward): its first tiles may load before the
+  // GEMM's dependency wait
+  bool w_static = false;
 };
+// Tensor-core GEMM when supported, else the CUDA-core one (capi.cu).
+// w_static: the weight is not written by the kernel launched just before on
+// the stream, so the tcgen05 GEMM may start loading it before its dependency
+// wait.
+int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
+                    int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale,
+                    int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
+                    int64_t ldy, cudaStream_t st, bool w_static = false);
 int gemm_tc_block_n(int64_t N);
 int gemm_tc_stats_width(int64_t N, int w_dtype);  // column width of one statistics segment
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,

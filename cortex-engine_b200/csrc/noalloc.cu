@@ -31,7 +31,7 @@ namespace ck {
 int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,
                     int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale,
                     int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
-                    int64_t ldy, cudaStream_t st);
+                    int64_t ldy, cudaStream_t st, bool w_static);
 }  // namespace ck
 
 namespace {
