@@ -9,6 +9,7 @@
 //                 argsort of :149 followed by :161)
 //
 // Device pipeline, no host synchronisation:
+//   0. zero     counts, flags and the rank matrix (one kernel, not memsets)
 //   1. count    warp-aggregated histogram (match_any) + sortedness flag
 //   2. scan     one CTA: exclusive scan of counts, e_max
 //   3. rank     (unsorted input only) per 256-event chunk: rank within the chunk
@@ -67,6 +68,19 @@ PackWs carve(void* ws, int64_t E, int32_t B) {
   p += align256((size_t)E * 4);
   w.matrix = reinterpret_cast<int32_t*>(p);
   return w;
+}
+
+// The counts, the flags and the rank matrix start at zero: one launch in
+// the stream's programmatic chain instead of three memsets.
+__global__ void pack_zero_kernel(int32_t* counts, int32_t B, int32_t* flag, int32_t* matrix,
+                                 int64_t matrix_words) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = i0; i < B; i += step) counts[i] = 0;
+  if (i0 < 64) flag[i0] = 0;
+  for (int64_t i = i0; i < matrix_words; i += step) matrix[i] = 0;
 }
 
 __global__ void pack_count_kernel(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
@@ -285,12 +299,16 @@ int pack_events(const void* bidx, int dt, int64_t stride, int64_t E, int32_t B,
   if (dt != CK_I64 && dt != CK_I32) return CK_ERR_UNSUPPORTED;
   if (ws_bytes < pack_workspace_bytes(E, B) || ws == nullptr) return CK_ERR_WORKSPACE;
   PackWs w = carve(ws, E, B);
-  if (cudaMemsetAsync(counts, 0, (size_t)B * 4, st) != cudaSuccess) return record_cuda_error();
-  if (cudaMemsetAsync(w.flag, 0, 256, st) != cudaSuccess) return record_cuda_error();
-  if (w.has_matrix && E > 0 &&
-      cudaMemsetAsync(w.matrix, 0, (size_t)B * w.nchunks * 4, st) != cudaSuccess)
-    return record_cuda_error();
   const int sms = num_sms();
+  {
+    const int64_t mwords = (w.has_matrix && E > 0) ? (int64_t)B * w.nchunks : 0;
+    int64_t blocks = ((B > mwords ? (int64_t)B : mwords) + 255) / 256;
+    if (blocks < 1) blocks = 1;
+    if (blocks > 4 * sms) blocks = 4 * sms;
+    if (launch_pdl(pack_zero_kernel, dim3((unsigned)blocks), dim3(256), 0, st, counts, B, w.flag,
+                   w.matrix, mwords))
+      return CK_ERR_CUDA;
+  }
   if (E > 0) {
     int64_t blocks = (E + 255) / 256;
     if (blocks > 8 * sms) blocks = 8 * sms;
