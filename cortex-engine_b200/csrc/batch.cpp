@@ -29,6 +29,15 @@ CK_SIMD_CLONES void narrow(const int64_t* src, int64_t n, int32_t* dst, int64_t*
   *mx_out = mx;
 }
 
+// Saturating int64 -> int32 narrowing alone (the arrays whose range the
+// caller does not need).
+CK_SIMD_CLONES void narrow_only(const int64_t* src, int64_t n, int32_t* dst) {
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t v = src[i];
+    dst[i] = (int32_t)(v < INT32_MIN ? INT32_MIN : (v > INT32_MAX ? INT32_MAX : v));
+  }
+}
+
 CK_SIMD_CLONES void minmax32(const int32_t* src, int64_t n, int64_t* mn_out, int64_t* mx_out) {
   int32_t mn = INT32_MAX, mx = INT32_MIN;
   for (int64_t i = 0; i < n; ++i) {
@@ -56,7 +65,10 @@ extern "C" int ck_batch_stage(const void* nid, const void* tb, const void* val, 
   for (int k = 0; k < 4 && E > 0; ++k) {
     int64_t mn, mx;
     if (idx_dtype == CK_I64) {
-      narrow(static_cast<const int64_t*>(src[k]), E, arr + k * capacity, &mn, &mx);
+      if (k == 3)  // only the batch indices' range is needed (B, validity)
+        narrow(static_cast<const int64_t*>(src[k]), E, arr + k * capacity, &mn, &mx);
+      else
+        narrow_only(static_cast<const int64_t*>(src[k]), E, arr + k * capacity);
     } else {
       std::memcpy(arr + k * capacity, src[k], (size_t)E * 4);
       if (k == 3) minmax32(static_cast<const int32_t*>(src[k]), E, &mn, &mx);
