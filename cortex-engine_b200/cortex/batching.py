@@ -109,22 +109,25 @@ class BatchRunner:
         """(B, behavior_dim) on the model's device from four host (E,) index tensors."""
         idx = (neuron_ids, time_bins, values, batch_indices)
         dt = neuron_ids.dtype
-        if dt not in (torch.int32, torch.int64) or any(x.dtype != dt for x in idx):
+        # (explicit comparisons: this runs once per request batch)
+        if ((dt is not torch.int64 and dt is not torch.int32) or time_bins.dtype is not dt
+                or values.dtype is not dt or batch_indices.dtype is not dt):
             dt = torch.int64
             idx = tuple(x.to(torch.int64) for x in idx)
-        if not all(x.is_contiguous() for x in idx):
-            idx = tuple(x.contiguous() for x in idx)
-        E = int(idx[0].shape[0])
+        n_, t_, v_, b_ = idx
+        if not (n_.is_contiguous() and t_.is_contiguous() and v_.is_contiguous()
+                and b_.is_contiguous()):
+            n_, t_, v_, b_ = (x.contiguous() for x in idx)
+        E = n_.shape[0]
         lib = L.load()
         with self._lock:
             m, dev, wdt = self.model.native_info()
             stream = L.stream_of(dev)
             a = self._arena(dev, stream, m)
             B = ctypes.c_int32(0)
-            rc = lib.ck_runner_stage(a.handle, idx[0].data_ptr(), idx[1].data_ptr(),
-                                     idx[2].data_ptr(), idx[3].data_ptr(),
-                                     L.CK_I64 if dt == torch.int64 else L.CK_I32, E,
-                                     int(batch_size) if batch_size is not None else 0,
+            rc = lib.ck_runner_stage(a.handle, n_.data_ptr(), t_.data_ptr(), v_.data_ptr(),
+                                     b_.data_ptr(), L.CK_I64 if dt is torch.int64 else L.CK_I32,
+                                     E, int(batch_size) if batch_size is not None else 0,
                                      ctypes.byref(B))
             L.check(rc, "ck_runner_stage")
             out = torch.empty(B.value, self._bdim, dtype=wdt, device=dev)

@@ -347,8 +347,8 @@ class CortexModel(nn.Module):
             raise ValueError(
                 f"shape mismatch: neuron_ids={neuron_ids.shape}, time_bins={time_bins.shape}, "
                 f"values={values.shape}, batch_indices={batch_indices.shape}")
-        if not return_aux and (neuron_ids.device.type == time_bins.device.type ==
-                               values.device.type == batch_indices.device.type == "cpu"):
+        if not return_aux and (neuron_ids.is_cpu and time_bins.is_cpu and values.is_cpu
+                               and batch_indices.is_cpu):
             # host indices: one packed int32 batch, one copy, one graph replay (the
             # weights' device is checked by the cached native description)
             return {"behavior": self.batch_runner().forward_host(
