@@ -19,8 +19,9 @@
 //                     hold vt_{h(p)} for the same pairs, and rows [NC, 2NC) hold
 //                     the bf16 remainders (value - bf16(value)) of rows [0, NC),
 //                     so hi + lo carries the fp32 weights into the bf16 MMA.
-//   head_kernel       one CTA per 128-latent tile, a cluster of ceil(L/128) CTAs
-//                     per sample. Each CTA applies the two LayerNorms to its rows
+//   head_kernel       one CTA per R-latent tile (R = 64 while ceil(L/64) <= 8,
+//                     else 128), a cluster of ceil(L/R) CTAs per sample; the MMA
+//                     runs M = 128 with zero rows. Each CTA applies the two LayerNorms to its rows
 //                     exactly as row_norm2 does (bf16 rounding after each), writes
 //                     them as the 128B-swizzled MMA A operand, multiplies by Qall
 //                     with tcgen05 into TMEM, then reduces the tile to per-pair
