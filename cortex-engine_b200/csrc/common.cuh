@@ -239,7 +239,6 @@ __device__ __forceinline__ void gelu32(float* v) {
         v[i] = gelu_as(v[i]);
     }
   } else {
-#pragma unroll
     gelu32_pairs(v);
   }
 }

@@ -13,12 +13,21 @@
 // (device count, padded batches) events n_valid..E-1 are padding: their ids
 // are not read and their rows are written as zeros, which keeps every row a
 // later kernel may touch finite.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace ck {
 
 namespace {
+
+// bf16x2 add, round to nearest even (sm_90+)
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 __device__ __forceinline__ int64_t load_idx(const void* p, int dt, int64_t i, int64_t stride) {
   if (dt == CK_I64) return reinterpret_cast<const int64_t*>(p)[i * stride];
@@ -78,6 +87,7 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
   grid_dep_wait();
   grid_dep_launch();
   constexpr int RPW = 32 / G;
+  constexpr bool kPair = std::is_same<T, __nv_bfloat16>::value && VEC == 8;
   const int lane = threadIdx.x & 31;
   const int sub = lane % G;
   const int slot = lane / G;
@@ -114,19 +124,34 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
 #pragma unroll
       for (int k = 0; k < VEC; ++k) x[i][k] = 0.f;
       if (ok && c < nvec) {
-        float fn[VEC], ft[VEC], fv[VEC];
-        if constexpr (VEC == 1) {
-          fn[0] = (float)ne[n * a.n_ld + c];
-          ft[0] = (float)te[t * a.t_ld + c];
-          fv[0] = (float)ve[v * a.v_ld + c];
+        if constexpr (kPair) {
+          // bf16(bf16(n + t) + v) on the bf16x2 adder: a correctly rounded bf16
+          // sum equals torch's fp32 add then bf16 round (fp32's 24 bits are at
+          // least 2 * 8 + 2, so the double rounding is innocuous)
+          const uint4 rn = *reinterpret_cast<const uint4*>(ne + n * a.n_ld + c * VEC);
+          const uint4 rt = *reinterpret_cast<const uint4*>(te + t * a.t_ld + c * VEC);
+          const uint4 rv = *reinterpret_cast<const uint4*>(ve + v * a.v_ld + c * VEC);
+          uint4 r;
+          r.x = badd2(badd2(rn.x, rt.x), rv.x);
+          r.y = badd2(badd2(rn.y, rt.y), rv.y);
+          r.z = badd2(badd2(rn.z, rt.z), rv.z);
+          r.w = badd2(badd2(rn.w, rt.w), rv.w);
+          unpack8(r, x[i]);
         } else {
-          Vec<T>::load(ne + n * a.n_ld + c * VEC, fn);
-          Vec<T>::load(te + t * a.t_ld + c * VEC, ft);
-          Vec<T>::load(ve + v * a.v_ld + c * VEC, fv);
-        }
+          float fn[VEC], ft[VEC], fv[VEC];
+          if constexpr (VEC == 1) {
+            fn[0] = (float)ne[n * a.n_ld + c];
+            ft[0] = (float)te[t * a.t_ld + c];
+            fv[0] = (float)ve[v * a.v_ld + c];
+          } else {
+            Vec<T>::load(ne + n * a.n_ld + c * VEC, fn);
+            Vec<T>::load(te + t * a.t_ld + c * VEC, ft);
+            Vec<T>::load(ve + v * a.v_ld + c * VEC, fv);
+          }
 #pragma unroll
-        for (int k = 0; k < VEC; ++k)
-          x[i][k] = Vec<T>::round(Vec<T>::round(fn[k] + ft[k]) + fv[k]);
+          for (int k = 0; k < VEC; ++k)
+            x[i][k] = Vec<T>::round(Vec<T>::round(fn[k] + ft[k]) + fv[k]);
+        }
       }
     }
     if (LN) {
@@ -141,14 +166,30 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
       for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       const float mean = s / (float)a.D;
       float q = 0.f;
+      const unsigned long long nmean2 = f2pk(-mean, -mean);
+      if constexpr (kPair) {  // even and odd columns on the paired fp32 pipe
+        unsigned long long q2 = f2pk(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i)
-        if (sub + G * i < nvec)
+        for (int i = 0; i < MAXV; ++i)
+          if (sub + G * i < nvec)
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) {
-            const float d = x[i][k] - mean;
-            q += d * d;
-          }
+            for (int k = 0; k < VEC; k += 2) {
+              const unsigned long long d = fadd2(f2pk(x[i][k], x[i][k + 1]), nmean2);
+              q2 = ffma2(d, d, q2);
+            }
+        float q0, q1;
+        f2up(q2, q0, q1);
+        q = q0 + q1;
+      } else {
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i)
+          if (sub + G * i < nvec)
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+              const float d = x[i][k] - mean;
+              q += d * d;
+            }
+      }
 #pragma unroll
       for (int o = G / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
       const float rstd = 1.0f / sqrtf(q / (float)a.D + a.eps);
@@ -158,7 +199,24 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
 #pragma unroll
         for (int i = 0; i < MAXV; ++i) {
           const int c = sub + G * i;
-          if (c < nvec) {
+          if (c < nvec && kPair) {
+            // ((x - mean) * rstd) * gamma + beta, two columns per instruction
+            // (the same operations and order as the scalar form below)
+            const uint4 gw = *reinterpret_cast<const uint4*>(g + c * VEC);
+            const uint4 bw = bt ? *reinterpret_cast<const uint4*>(bt + c * VEC)
+                                : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t gv[4] = {gw.x, gw.y, gw.z, gw.w};
+            const uint32_t bv[4] = {bw.x, bw.y, bw.z, bw.w};
+            const unsigned long long rstd2 = f2pk(rstd, rstd);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              unsigned long long y = fadd2(f2pk(x[i][2 * k], x[i][2 * k + 1]), nmean2);
+              y = fmul2(y, rstd2);
+              y = ffma2(y, f2pk(bf16_lo(gv[k]), bf16_hi(gv[k])),
+                        f2pk(bf16_lo(bv[k]), bf16_hi(bv[k])));
+              f2up(y, x[i][2 * k], x[i][2 * k + 1]);
+            }
+          } else if (c < nvec) {
             float gk[VEC], bk[VEC];
             if constexpr (VEC == 1) {
               gk[0] = (float)g[c];
