@@ -169,37 +169,57 @@ __device__ __forceinline__ void merge3(float& m, float& s, float& w, float m2, f
   m = mn;
 }
 
-// LayerNorm of a row held as MAXV 8-wide vectors per lane (same arithmetic as
-// row_norm_kernel's layer_norm_regs followed by the gamma/beta step).
-template <int MAXV>
-__device__ __forceinline__ void ln_lane_row(float (&v)[MAXV][8], const uint4 (&g)[MAXV],
-                                            const uint4 (&bt)[MAXV], bool has_b, int D,
-                                            float eps) {
-  float s = 0.f;
+// LayerNorms of NR rows held as MAXV 8-wide vectors per lane, one warp (per
+// row the arithmetic of row_norm_kernel's layer_norm_regs followed by the
+// gamma/beta step), the rows' reductions interleaved so that one row's
+// shuffle latency covers the others'.
+template <int MAXV, int NR>
+__device__ __forceinline__ void ln_lane_rows(float (&v)[NR][MAXV][8], const uint4 (&g)[MAXV],
+                                             const uint4 (&bt)[MAXV], bool has_b, int D,
+                                             float eps) {
+  float s[NR], mean[NR], q[NR], rstd[NR];
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i)
+  for (int j = 0; j < NR; ++j) {
+    s[j] = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) s += v[i][k];
-  const float mean = warp_sum(s) / (float)D;
-  float q = 0.f;
+    for (int i = 0; i < MAXV; ++i)
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i)
+      for (int k = 0; k < 8; ++k) s[j] += v[j][i][k];
+  }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float d = v[i][k] - mean;
-      q += d * d;
-    }
-  const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)D + eps);
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < NR; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+#pragma unroll
+  for (int j = 0; j < NR; ++j) {
+    mean[j] = s[j] / (float)D;
+    q[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float d = v[j][i][k] - mean[j];
+        q[j] += d * d;
+      }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < NR; ++j) q[j] += __shfl_xor_sync(0xffffffffu, q[j], o);
+#pragma unroll
+  for (int j = 0; j < NR; ++j) rstd[j] = 1.0f / sqrtf(q[j] / (float)D + eps);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     float gf[8], bf[8];
     unpack8(g[i], gf);
     unpack8(bt[i], bf);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      v[i][k] = (v[i][k] - mean) * rstd;
-      v[i][k] = v[i][k] * gf[k] + (has_b ? bf[k] : 0.f);
-    }
+    for (int j = 0; j < NR; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[j][i][k] = (v[j][i][k] - mean[j]) * rstd[j];
+        v[j][i][k] = v[j][i][k] * gf[k] + (has_b ? bf[k] : 0.f);
+      }
   }
 }
 
@@ -232,7 +252,7 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* part = reinterpret_cast<float*>(misc + 256);  // [PH][3] this CTA's partials
   float* ofin = part + PH * 3;                         // [PH]
-  // [4 warps][PH][3] per-warp partials; the A tile is dead once the MMAs are done
+  // [4 lane quarters][PH][3] partials; the A tile is dead once the MMAs are done
   float* red = reinterpret_cast<float*>(sA);
 
   const int tid = threadIdx.x;
@@ -299,29 +319,43 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1)
       b2[i] = p.b2 ? reinterpret_cast<const uint4*>(p.b2)[c] : z;
     }
     const bool landed = mbar_wait(xfull, 0, abort_flag, 20);
-    for (int r = warp; r < p.R; r += HEAD_THREADS / 32) {
-      uint4* slot[MAXV];
+    // rows r0 + j * NW, j < NRP, per pass (R is 64 or 128, so all are below
+    // R; D = 768 keeps one row per pass inside the register budget); a row
+    // past the sample's end is normalised as zeros and stored as zeros
+    constexpr int NW = HEAD_THREADS / 32;
+    constexpr int NRP = MAXV <= 2 ? 2 : 1;
+    for (int r0 = warp; r0 < p.R; r0 += NRP * NW) {
+      uint4* slot[NRP][MAXV];
+      bool live[NRP];
+      float v[NRP][MAXV][8];
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i) {
-        const int c = lane + 32 * i;  // 16-byte chunk of the row
-        slot[i] = reinterpret_cast<uint4*>(sA + (c >> 3) * A_KB_BYTES + sw128_off(r, c & 7));
+      for (int j = 0; j < NRP; ++j) {
+        const int r = r0 + j * NW;
+        live[j] = landed && r < rows;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+          const int c = lane + 32 * i;  // 16-byte chunk of the row
+          slot[j][i] = reinterpret_cast<uint4*>(sA + (c >> 3) * A_KB_BYTES + sw128_off(r, c & 7));
+          if (live[j]) {
+            unpack8(*slot[j][i], v[j][i]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[j][i][k] = 0.f;
+          }
+        }
       }
-      if (landed && r < rows) {
-        float v[MAXV][8];
+      ln_lane_rows<MAXV, NRP>(v, g1, b1, p.b1 != nullptr, D, p.eps);
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) unpack8(*slot[i], v[i]);
-        ln_lane_row<MAXV>(v, g1, b1, p.b1 != nullptr, D, p.eps);
+      for (int j = 0; j < NRP; ++j)
 #pragma unroll
         for (int i = 0; i < MAXV; ++i)
 #pragma unroll
-          for (int k = 0; k < 8; ++k) v[i][k] = rbf(v[i][k]);
-        ln_lane_row<MAXV>(v, g2, b2, p.b2 != nullptr, D, p.eps);
+          for (int k = 0; k < 8; ++k) v[j][i][k] = rbf(v[j][i][k]);
+      ln_lane_rows<MAXV, NRP>(v, g2, b2, p.b2 != nullptr, D, p.eps);
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) *slot[i] = pack8(v[i]);
-      } else {
+      for (int j = 0; j < NRP; ++j)
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) *slot[i] = z;
-      }
+        for (int i = 0; i < MAXV; ++i) *slot[j][i] = live[j] ? pack8(v[j][i]) : z;
     }
   }
   fence_proxy_async_smem();
@@ -369,14 +403,17 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1)
     }
   }
 
-  // Epilogue (warps 0-3, one latent row per thread): per-pair tile partials.
-  if (warp < 4) {
+  // Epilogue (one latent row per thread): per-pair tile partials. The four
+  // warps of a TMEM lane quarter (warp % 4) share its rows and take every
+  // fourth pair each.
+  {
+    const int quarter = warp & 3, slice = warp >> 2;
     const bool got = mbar_wait(done, 0, abort_flag, 24);
     __syncwarp();
     tc_fence_after();
-    const int r = warp * 32 + lane;
+    const int r = quarter * 32 + lane;
     const bool valid = got && r < rows;
-    const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16);
+    const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16);
     float val[NC];
 #pragma unroll
     for (int c0 = 0; c0 < NC; c0 += 32) {
@@ -388,18 +425,19 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1)
       for (int i = 0; i < 32; ++i) val[c0 + i] = hi[i] + lo[i];
     }
     const int HQ = p.H * p.nq;
+    static_assert(HEAD_THREADS / 32 == 16, "four warps per TMEM lane quarter");
 #pragma unroll
     for (int q = 0; q < PH; ++q) {
-      if (q < HQ) {
+      if (q < HQ && (q & 3) == slice) {
         const float s = valid ? val[q] : -INFINITY;
         const float m = warp_max(s);
         const float e = valid ? ex2(s - m) : 0.f;
         const float se = warp_sum(e);
         const float we = warp_sum(e * val[PH + q]);
         if (lane == 0) {
-          red[(warp * PH + q) * 3 + 0] = m;
-          red[(warp * PH + q) * 3 + 1] = se;
-          red[(warp * PH + q) * 3 + 2] = we;
+          red[(quarter * PH + q) * 3 + 0] = m;
+          red[(quarter * PH + q) * 3 + 1] = se;
+          red[(quarter * PH + q) * 3 + 2] = we;
         }
       }
     }
