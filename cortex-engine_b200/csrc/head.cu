@@ -250,6 +250,7 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1)
   uint64_t* xfull = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* mma_ok = reinterpret_cast<int*>(tmem_slot + 2);  // the MMAs completed
   float* part = reinterpret_cast<float*>(misc + 256);  // [PH][3] this CTA's partials
   float* ofin = part + PH * 3;                         // [PH]
   // [4 lane quarters][PH][3] partials; the A tile is dead once the MMAs are done
@@ -406,10 +407,13 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1)
   // Epilogue (one latent row per thread): per-pair tile partials. The four
   // warps of a TMEM lane quarter (warp % 4) share its rows and take every
   // fourth pair each.
+  // Only the MMA thread waits on `done`; the other warps wait at the barrier
+  // instead of polling the mbarrier beside the MMAs' shared-memory reads.
+  if (tid == 128) *mma_ok = mbar_wait(done, 0, abort_flag, 24) ? 1 : 0;
+  __syncthreads();
   {
     const int quarter = warp & 3, slice = warp >> 2;
-    const bool got = mbar_wait(done, 0, abort_flag, 24);
-    __syncwarp();
+    const bool got = *mma_ok != 0;
     tc_fence_after();
     const int r = quarter * 32 + lane;
     const bool valid = got && r < rows;
