@@ -30,14 +30,12 @@ SOURCES = [
     "tokenizer.cu",
     "norm.cu",
     "gemm_tc.cu",
-    "gemm_chain.cu",
     "gemm_simt.cu",
     "attention_tc.cu",
     "attention_ws.cu",
     "attention_simt.cu",
     "capi.cu",
     "head.cu",
-    "fold.cu",
     "forward.cu",
     "noalloc.cu",
     "batch.cpp",

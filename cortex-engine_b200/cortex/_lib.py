@@ -62,17 +62,12 @@ class LinearWeight(ctypes.Structure):
     _fields_ = [("w", _vp), ("dtype", _int), ("scale", _vp), ("bias", _vp)]
 
 
-class NormFold(ctypes.Structure):
-    _fields_ = [("w", _vp), ("colsum", _vp), ("bias", _vp)]
-
-
 class BlockWeights(ctypes.Structure):
     _fields_ = [
         ("norm_attn_w", _vp), ("norm_attn_b", _vp),
         ("qkv", LinearWeight), ("out", LinearWeight),
         ("norm_mlp_w", _vp), ("norm_mlp_b", _vp),
         ("mlp0", LinearWeight), ("mlp2", LinearWeight),
-        ("qkv_fold", NormFold), ("mlp0_fold", NormFold),
     ]
 
 
@@ -119,7 +114,6 @@ _SIGS = {
                                      _int, _int, _i64, _i64, _vp, _int, _vp, _i64, _i64, _vp,
                                      _i64, _vp]),
     "ck_attention": (_int, [ctypes.POINTER(AttentionArgs), _vp]),
-    "ck_norm_fold_weights": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ck_forward_workspace_bytes": (_sz, [ctypes.POINTER(Model), _i64, _i32]),
     "ck_forward": (_int, [ctypes.POINTER(Model), _vp, _vp, _vp, _vp, _int, _i64, _i32, _vp, _vp,
                           _sz, _vp]),

@@ -91,8 +91,6 @@ class BatchRunner:
         """The arena of (dev, stream), holding the model's current description m."""
         model = self.model
         native = model._native
-        if native[2]:
-            model._refresh_folds()
         a = self._arenas.get((dev, stream))
         if a is None:
             a = _Arena(dev, m)

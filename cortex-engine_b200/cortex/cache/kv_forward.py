@@ -56,7 +56,6 @@ def forward_with_kv_cache(model, windows: list[dict], cache) -> torch.Tensor:
     miss = [b for b in range(B) if not hit[b]]
 
     m = model.native_model()
-    model._refresh_folds()
     lib = L.load()
     stream = L.stream_of(dev)
     E_all = int(counts.sum())

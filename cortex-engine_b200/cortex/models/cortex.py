@@ -19,7 +19,6 @@ from __future__ import annotations
 
 import ctypes
 import operator
-import os
 import threading
 from typing import cast
 
@@ -175,7 +174,6 @@ class CortexModel(nn.Module):
                 return self._native[0]
             key = self._state_key()
             keep: list = []
-            folds: list = []
             cfg = self.config
             tok, enc, head = self.tokenizer, self.encoder, self.behavior_head
             dt = tok.neuron_emb.weight.dtype
@@ -222,8 +220,6 @@ class CortexModel(nn.Module):
                 b.qkv, b.out = self._lw(blk.qkv_proj, keep), self._lw(blk.out_proj, keep)
                 b.norm_mlp_w, b.norm_mlp_b = t(blk.norm_mlp.weight), t(blk.norm_mlp.bias)
                 b.mlp0, b.mlp2 = self._lw(blk.mlp[0], keep), self._lw(blk.mlp[2], keep)
-                b.qkv_fold = self._fold(blk.norm_attn, blk.qkv_proj, keep, folds)
-                b.mlp0_fold = self._fold(blk.norm_mlp, blk.mlp[0], keep, folds)
             keep.append(blocks)
             m.blocks = ctypes.cast(blocks, ctypes.POINTER(L.BlockWeights))
             m.final_norm_w, m.final_norm_b = t(enc.final_norm.weight), t(enc.final_norm.bias)
@@ -232,7 +228,7 @@ class CortexModel(nn.Module):
             m.head_q, m.head_kv, m.head_out = (self._lw(head.q_proj, keep),
                                                self._lw(head.kv_proj, keep),
                                                self._lw(head.out_proj, keep))
-            self._native = (m, keep, folds, tok.neuron_emb.weight.device, dt)
+            self._native = (m, keep, None, tok.neuron_emb.weight.device, dt)
             self._native_key = key
             self._native_epoch = _REGISTRATIONS[0]
             return m
@@ -244,57 +240,8 @@ class CortexModel(nn.Module):
         n = self._native
         return n[0], n[3], n[4]
 
-    # LayerNorm folds (ck_norm_fold_weights): norm_attn into qkv_proj and norm_mlp
-    # into mlp.0, for bf16 weights. The folded weight is derived data; it is
-    # rebuilt whenever the version counter of the norm or the linear weight moves
-    # (in-place optimizer updates, copy_ under no_grad). Writes through ``.data``
-    # bypass version counters: call ``invalidate_native()`` after those.
-
-    def _fold(self, norm: nn.Module, lin: nn.Module, keep: list, folds: list) -> L.NormFold:
-        nf = L.NormFold()
-        if os.environ.get("CK_NORM_FOLD") != "1":  # folding is opt-in (see ck_forward)
-            return nf
-        w = getattr(lin, "weight", None)
-        if (w is None or w.dtype != torch.bfloat16 or getattr(lin, "bias", None) is not None
-                or w.dim() != 2 or w.shape[1] % 8 != 0 or not w.is_contiguous()
-                or norm.weight.dtype != torch.bfloat16):
-            return nf
-        N, K = w.shape
-        wf = torch.empty(N, K, dtype=torch.bfloat16, device=w.device)
-        cs = torch.empty(N, dtype=torch.float32, device=w.device)
-        bw = torch.empty(N, dtype=torch.float32, device=w.device)
-        entry = [norm, lin, wf, cs, bw, None]
-        self._run_fold(entry)
-        keep.extend((wf, cs, bw))
-        folds.append(entry)
-        nf.w, nf.colsum, nf.bias = wf.data_ptr(), cs.data_ptr(), bw.data_ptr()
-        return nf
-
-    @staticmethod
-    def _fold_version(entry) -> tuple:
-        norm, lin = entry[0], entry[1]
-        return (norm.weight._version, -1 if norm.bias is None else norm.bias._version,
-                lin.weight._version)
-
-    def _run_fold(self, entry) -> None:
-        norm, lin, wf, cs, bw = entry[:5]
-        w = lin.weight
-        g = norm.weight.contiguous()
-        b = None if norm.bias is None else norm.bias.contiguous()
-        rc = L.load().ck_norm_fold_weights(
-            w.data_ptr(), w.shape[0], w.shape[1], w.stride(0), g.data_ptr(),
-            None if b is None else b.data_ptr(), wf.data_ptr(), cs.data_ptr(), bw.data_ptr(),
-            L.stream_of(w.device))
-        L.check(rc, "ck_norm_fold_weights")
-        entry[5] = self._fold_version(entry)
-
-    def _refresh_folds(self) -> None:
-        for entry in self._native[2]:
-            if entry[5] != self._fold_version(entry):
-                self._run_fold(entry)
-
     def invalidate_native(self) -> None:
-        """Drop the cached weight description (and the derived LayerNorm folds)."""
+        """Drop the cached weight description."""
         self._native = None
 
     def forward_packed(self, packed) -> dict[str, torch.Tensor]:
@@ -369,7 +316,6 @@ class CortexModel(nn.Module):
             return self._forward_modules(*idx, batch_size=batch_size)
 
         m = self.native_model()
-        self._refresh_folds()
         lib = L.load()
         nbytes = lib.ck_forward_workspace_bytes(ctypes.byref(m), E, batch_size)
         ws = self.workspace(dev, nbytes)

@@ -20,76 +20,22 @@ copy of it ever exists. Activations stay in their dtype (the reference's
 activation scale is computed but never used in the forward pass, :17-19). CUDA
 only.
 
-The calibration helpers (activation statistics, hooks, ``derive_scales``) are
-plain torch utilities with the reference's semantics.
+Activation calibration (hooks, percentile statistics, summaries) and the
+checkpoint helpers of the reference module are not on the forward path and are
+not part of this package; a model quantized with the reference's tools loads
+here through ``convert_model`` and ``load_state_dict``.
 """
 
 from __future__ import annotations
 
 import copy
-from dataclasses import dataclass, field
-from pathlib import Path
-from typing import Any
+from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
 
 from cortex import _lib as L
 from cortex.kernels import _ops
-
-
-@dataclass
-class ActivationStats:
-    """Per-layer activation statistics (cortex/quantization/calibrate.py:55-79)."""
-
-    abs_max_history: list[float] = field(default_factory=list)
-
-    def update(self, x: torch.Tensor) -> None:
-        self.abs_max_history.append(float(x.detach().abs().max().item()))
-
-    @property
-    def percentile_99(self) -> float:
-        if not self.abs_max_history:
-            return 1.0
-        vals = sorted(self.abs_max_history)
-        idx = max(0, int(len(vals) * 0.99) - 1)
-        return vals[idx]
-
-    @property
-    def n_batches(self) -> int:
-        return len(self.abs_max_history)
-
-
-class CalibrationHook:
-    """Forward pre-hook recording input statistics (:82-96)."""
-
-    def __init__(self) -> None:
-        self.stats = ActivationStats()
-        self._handle: Any = None
-
-    def __call__(self, module: nn.Module, args: tuple[Any, ...]) -> None:
-        if args:
-            self.stats.update(args[0])
-
-    def remove(self) -> None:
-        if self._handle is not None:
-            self._handle.remove()
-            self._handle = None
-
-
-def attach_calibration_hooks(model: nn.Module) -> dict[str, CalibrationHook]:
-    hooks: dict[str, CalibrationHook] = {}
-    for name, module in model.named_modules():
-        if isinstance(module, nn.Linear):
-            hook = CalibrationHook()
-            hook._handle = module.register_forward_pre_hook(hook)
-            hooks[name] = hook
-    return hooks
-
-
-def remove_calibration_hooks(hooks: dict[str, CalibrationHook]) -> None:
-    for hook in hooks.values():
-        hook.remove()
 
 
 @dataclass
@@ -103,19 +49,6 @@ class LayerScales:
 def weight_scales(weight: torch.Tensor) -> torch.Tensor:
     """``absmax_row / 127`` clamped at 1e-8, in fp32 (:154)."""
     return weight.detach().float().abs().amax(dim=1).clamp(min=1e-8) / 127.0
-
-
-def derive_scales(model: nn.Module, hooks: dict[str, CalibrationHook]) -> dict[str, LayerScales]:
-    scales: dict[str, LayerScales] = {}
-    for name, module in model.named_modules():
-        if not isinstance(module, nn.Linear) or name not in hooks:
-            continue
-        hook = hooks[name]
-        if hook.stats.n_batches == 0:
-            continue
-        scales[name] = LayerScales(weight_scale=weight_scales(module.weight).cpu(),
-                                   act_scale=max(hook.stats.percentile_99, 1e-8) / 127.0)
-    return scales
 
 
 class QuantizedLinear(nn.Module):
@@ -176,47 +109,3 @@ def _replace_linears(module: nn.Module, scales: dict[str, LayerScales], prefix: 
             setattr(module, name, QuantizedLinear.from_linear(child, scales[full_name]))
         else:
             _replace_linears(child, scales, full_name)
-
-
-def model_weight_bytes(model: nn.Module) -> int:
-    total = 0
-    for p in model.parameters():
-        total += p.numel() * p.element_size()
-    for buf in model.buffers():
-        total += buf.numel() * buf.element_size()
-    return total
-
-
-def count_quantized_linears(model: nn.Module) -> tuple[int, int]:
-    n_quant = sum(1 for m in model.modules() if isinstance(m, QuantizedLinear))
-    n_float = sum(1 for m in model.modules() if isinstance(m, nn.Linear))
-    return n_quant, n_quant + n_float
-
-
-def save_quantized(model: nn.Module, path: Path, meta: dict[str, Any] | None = None) -> None:
-    """``torch.save({'state_dict': ..., 'meta': ...})`` (:305-318)."""
-    path = Path(path)
-    path.parent.mkdir(parents=True, exist_ok=True)
-    torch.save({"state_dict": model.state_dict(), "meta": meta or {}}, path)
-
-
-def load_quantized(path: Path, model: nn.Module) -> nn.Module:
-    payload = torch.load(path, map_location="cpu", weights_only=True)
-    model.load_state_dict(payload["state_dict"])
-    return model
-
-
-def calibration_summary(hooks: dict[str, CalibrationHook],
-                        scales: dict[str, LayerScales]) -> list[dict[str, Any]]:
-    rows = []
-    for name, hook in hooks.items():
-        s = scales.get(name)
-        rows.append({
-            "layer": name,
-            "calib_batches": hook.stats.n_batches,
-            "act_abs_max_p99": round(hook.stats.percentile_99, 6),
-            "act_scale": round(s.act_scale, 8) if s else None,
-            "weight_scale_min": round(float(s.weight_scale.min()), 8) if s else None,
-            "weight_scale_max": round(float(s.weight_scale.max()), 8) if s else None,
-        })
-    return rows

@@ -24,7 +24,7 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
   if (w_dtype == CK_I8 && (w_scale == nullptr || w_layout != CK_W_NK)) return CK_ERR_INVALID_ARG;
   if (dtype == CK_BF16 && gemm_tc_supported(M, K, lda, w_dtype, w_layout, N, ldw, A, W, ldy, Y,
                                             epi, aux, ld_aux)) {
-    GemmFusion fz = {nullptr, nullptr, 0, 0.f, nullptr, nullptr};
+    GemmFusion fz;
     fz.w_static = w_static;
     return gemm_tc(A, M, K, lda, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux, ld_aux,
                    aux_row_mod, Y, ldy, st, w_static ? &fz : nullptr);

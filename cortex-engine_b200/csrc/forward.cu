@@ -7,9 +7,8 @@
 //   kv_proj         packed (E, 2D) keys|values                 (perceiver.py:67-69)
 //   cross attention varlen keys per sample, no padding          (perceiver.py:71-80)
 //   out_proj+resid  latents param broadcast as the residual      (perceiver.py:82)
-//   N x block       LN, qkv, attention, out+resid, LN, mlp0+GELU, mlp2+resid; with
-//                   ck_norm_fold weights both LNs fold into qkv / mlp0 (their
-//                   producers emit row statistics) and no normalised copy exists
+//   N x block       LN, qkv, attention, out+resid, LN, mlp0+GELU, mlp2+resid; each
+//                   LN rides the residual GEMM before it as a second output
 //   final LN + head LN, head q, head kv_proj, 2-query attention, out_proj D->1
 //                   (cortex.py:29-53): bf16 models run it as one fused kernel on a
 //                   weight-only matrix built per forward (head.cu); otherwise
@@ -38,28 +37,8 @@ size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
   size_t counts, offsets, dest, emax, packws, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
-      qall, stats, chain, chain_stride, chain_bytes, total;
+      qall, total;
 };
-
-// Chained GEMM launches per forward at most: a chain holds at least two
-// linears, and the forward has 2 + 4 * num_layers of them after the cross
-// attention.
-int64_t max_chains(const ck_model* m) { return 2 * (int64_t)m->num_layers + 2; }
-
-// Per-row LayerNorm statistics segments of a (., D) residual GEMM output.
-int64_t stats_segments(int64_t D) {
-  const int64_t sw = gemm_tc_stats_width(D, CK_BF16);
-  return (D + sw - 1) / sw;
-}
-
-// LayerNorm folding into qkv_proj / mlp.0 (ck_norm_fold) is opt-in with
-// CK_NORM_FOLD=1 in the environment. Measured on B200 (Cortex-S, bf16) the
-// folded epilogues (statistics in the residual GEMMs, the norm in qkv / mlp.0)
-// cost more GEMM time than the separate bf16 LayerNorm kernels they replace.
-bool norm_fold_enabled() {
-  const char* v = std::getenv("CK_NORM_FOLD");
-  return v != nullptr && std::strcmp(v, "1") == 0;
-}
 
 // The fused behaviour head (head.cu) runs whenever the model qualifies;
 // CK_HEAD_FUSED=0 in the environment selects the composed head instead.
@@ -96,10 +75,6 @@ Layout plan(const ck_model* m, int64_t E, int32_t B) {
   o.qh = take((size_t)m->behavior_dim * D * es);
   o.oh = take((size_t)B * m->behavior_dim * D * es);
   o.qall = take(use_fused_head(m) ? head_qall_bytes(m) : 1);
-  o.stats = take((size_t)stats_segments(D) * BL * sizeof(float2));
-  o.chain_stride = al(gemm_chain_counter_bytes((int64_t)BL, 4));
-  o.chain_bytes = o.chain_stride * (size_t)max_chains(m);
-  o.chain = take(o.chain_bytes);
   o.total = p;
   return o;
 }
@@ -169,41 +144,6 @@ SideStream* side_stream() {
   return &ss;
 }
 
-// Can this residual linear emit row statistics (bf16 weights, tensor-core GEMM)?
-bool resid_tc_ok(const ck_model* m, const ck_linear_weight& w, int64_t M, int64_t K, int64_t N,
-                 const void* A, const void* aux, int64_t ld_aux, const void* Y) {
-  if (m->dtype != CK_BF16 || w.w == nullptr || w.bias != nullptr || w.dtype != CK_BF16)
-    return false;
-  return gemm_tc_supported(M, K, K, w.dtype, CK_W_NK, N, K, A, w.w, N, Y, CK_EPI_RESID, aux,
-                           ld_aux);
-}
-
-// Can this norm + linear pair run folded?
-bool fold_tc_ok(const ck_model* m, const ck_norm_fold& f, const ck_linear_weight& w, int64_t M,
-                int64_t K, int64_t N, const void* A, int epi, const void* Y) {
-  if (!norm_fold_enabled() || m->dtype != CK_BF16) return false;
-  if (f.w == nullptr || f.colsum == nullptr || f.bias == nullptr || w.bias != nullptr) return false;
-  if (!al16(f.colsum) || !al16(f.bias)) return false;
-  return gemm_tc_supported(M, K, K, CK_BF16, CK_W_NK, N, K, A, f.w, N, Y, epi, nullptr, 0);
-}
-
-int lin_stats(const ck_model* m, const void* A, int64_t M, int64_t K, const ck_linear_weight& w,
-              int64_t N, const void* aux, int64_t ld_aux, int64_t mod, void* Y, void* stats,
-              cudaStream_t st) {
-  GemmFusion fz = {stats, nullptr, 0, 0.f, nullptr, nullptr};
-  fz.w_static = true;
-  return gemm_tc(A, M, K, K, w.w, w.dtype, CK_W_NK, N, K, w.scale, CK_EPI_RESID, aux, ld_aux, mod,
-                 Y, N, st, &fz);
-}
-
-int lin_folded(const void* A, int64_t M, int64_t K, const ck_norm_fold& f, int64_t N, int epi,
-               const void* stats, void* Y, cudaStream_t st) {
-  GemmFusion fz = {nullptr, stats, gemm_tc_stats_width(K, CK_BF16), 1e-5f, f.colsum, f.bias};
-  fz.w_static = true;
-  return gemm_tc(A, M, K, K, f.w, CK_BF16, CK_W_NK, N, K, nullptr, epi, nullptr, 0, 0, Y, N, st,
-                 &fz);
-}
-
 // LayerNorm fused into the residual GEMM before it (gemm_tc FUSE_LN) is on by
 // default; CK_LN_FUSE=0 in the environment runs separate LayerNorm kernels.
 bool ln_fuse_enabled() {
@@ -224,7 +164,12 @@ int lin_resid_ln(const ck_model* m, const void* A, int64_t M, int64_t K,
       (b == nullptr || al16(b)) && al16(X) &&
       gemm_tc_supported(M, K, K, w.dtype, CK_W_NK, N, K, A, w.w, N, Y, CK_EPI_RESID, aux,
                         ld_aux)) {
-    GemmFusion fz = {nullptr, nullptr, 0, kLnEps, nullptr, nullptr, X, N, g, b};
+    GemmFusion fz;
+    fz.eps = kLnEps;
+    fz.ln_out = X;
+    fz.ln_ld = N;
+    fz.ln_gamma = g;
+    fz.ln_beta = b;
     fz.w_static = true;
     return gemm_tc(A, M, K, K, w.w, w.dtype, CK_W_NK, N, K, w.scale, CK_EPI_RESID, aux, ld_aux,
                    mod, Y, N, st, &fz);
@@ -232,116 +177,6 @@ int lin_resid_ln(const ck_model* m, const void* A, int64_t M, int64_t K,
   const int rc = lin(m, A, M, K, K, w, N, CK_EPI_RESID, aux, ld_aux, mod, Y, N, st);
   if (rc != CK_OK) return rc;
   return row_norm(Y, m->dtype, M, (int32_t)N, N, g, b, kLnEps, CK_NORM_LAYER, X, N, st);
-}
-
-// Linears of the latent stack queued into chained launches (gemm_chain.cu).
-// Consecutive linears, each reading its predecessor's output, join one chain
-// of up to four; a linear the chain kernel does not take (int8 or biased
-// weights, odd shapes) ends the chain and runs on its own, as does a chain of
-// one. Each launch takes the next zeroed counter region of the workspace.
-class LinQueue {
- public:
-  LinQueue(const ck_model* m, int64_t M, uint8_t* ctr, size_t stride, int64_t regions,
-           cudaStream_t st)
-      : m_(m), M_(M), ctr_(ctr), stride_(stride), regions_(regions), st_(st) {}
-
-  int add(ChainLinear c, const ck_linear_weight& w) {
-    // the residual's producer, when it is queued: the last link writing it
-    c.aux_link = -1;
-    for (int i = n_ - 1; i >= 0 && c.kind >= CK_CHAIN_RESID; --i)
-      if (q_[i].Y == c.aux) {
-        c.aux_link = i;
-        break;
-      }
-    const bool follows = n_ > 0 && (c.A == q_[n_ - 1].Y || c.A == q_[n_ - 1].Y2);
-    if (n_ > 0 && (!follows || n_ == 4)) {
-      int rc = flush();
-      if (rc != CK_OK) return rc;
-      c.aux_link = -1;
-    }
-    ChainLinear alone = c;
-    alone.aux_link = -1;
-    const bool ok = w.dtype == CK_BF16 && w.bias == nullptr && m_->dtype == CK_BF16 &&
-                    gemm_chain_supported(&alone, 1, M_);
-    if (!ok) {
-      int rc = flush();
-      if (rc != CK_OK) return rc;
-      return run_alone(c, w);
-    }
-    q_[n_] = c;
-    w_[n_] = &w;
-    ++n_;
-    return CK_OK;
-  }
-
-  int flush() {
-    const int n = n_;
-    n_ = 0;
-    if (n == 0) return CK_OK;
-    if (n >= 2 && used_ < regions_ && gemm_chain_supported(q_, n, M_)) {
-      int* ctr = reinterpret_cast<int*>(ctr_ + stride_ * (size_t)used_++);
-      const int rc = gemm_chain(q_, n, M_, ctr, st_);
-      if (rc != CK_ERR_UNSUPPORTED) return rc;  // (no resident cluster count: launch singly)
-    }
-    for (int i = 0; i < n; ++i) {
-      const int rc = run_alone(q_[i], *w_[i]);
-      if (rc != CK_OK) return rc;
-    }
-    return CK_OK;
-  }
-
- private:
-  int run_alone(const ChainLinear& c, const ck_linear_weight& w) {
-    switch (c.kind) {
-      case CK_CHAIN_STORE:
-        return lin(m_, c.A, M_, c.K, c.lda, w, c.N, CK_EPI_STORE, nullptr, 0, 0, c.Y, c.ldy, st_);
-      case CK_CHAIN_GELU:
-        return lin(m_, c.A, M_, c.K, c.lda, w, c.N, CK_EPI_GELU, nullptr, 0, 0, c.Y, c.ldy, st_);
-      case CK_CHAIN_RESID:
-        return lin(m_, c.A, M_, c.K, c.lda, w, c.N, CK_EPI_RESID, c.aux, c.ld_aux, c.aux_row_mod,
-                   c.Y, c.ldy, st_);
-      default:
-        return lin_resid_ln(m_, c.A, M_, c.K, w, c.N, c.aux, c.ld_aux, c.aux_row_mod, c.Y,
-                            c.ln_gamma, c.ln_beta, c.Y2, st_);
-    }
-  }
-
-  const ck_model* m_;
-  int64_t M_;
-  uint8_t* ctr_;
-  size_t stride_;
-  int64_t regions_;
-  cudaStream_t st_;
-  ChainLinear q_[4];
-  const ck_linear_weight* w_[4] = {nullptr, nullptr, nullptr, nullptr};
-  int n_ = 0;
-  int64_t used_ = 0;
-};
-
-// One linear of the stack: (M, K) A with row stride K, (N, K) weight, output
-// row stride N.
-ChainLinear chain_link(int kind, const void* A, int64_t K, int64_t N, const void* W, void* Y,
-                       const void* aux = nullptr, int64_t ld_aux = 0, int64_t mod = 0,
-                       void* Y2 = nullptr, const void* g = nullptr, const void* b = nullptr) {
-  ChainLinear c;
-  c.kind = kind;
-  c.A = A;
-  c.lda = K;
-  c.W = W;
-  c.N = N;
-  c.K = K;
-  c.aux = aux;
-  c.ld_aux = ld_aux;
-  c.aux_row_mod = mod;
-  c.aux_link = -1;
-  c.Y = Y;
-  c.ldy = N;
-  c.Y2 = Y2;
-  c.ldy2 = N;
-  c.ln_gamma = g;
-  c.ln_beta = b;
-  c.eps = kLnEps;
-  return c;
 }
 
 ck_attention_args attn_base(const ck_model* m) {
@@ -412,11 +247,6 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
   } while (0)
 
   cudaEvent_t join_ev = nullptr;  // the side stream's prologue is done
-  // chained GEMM launches for the latent stack: their counters start at zero
-  const bool chains = io.stage != kKvOnly && m->num_layers > 0 && m->dtype == CK_BF16 &&
-                      gemm_chain_enabled() && !norm_fold_enabled();
-  if (chains && cudaMemsetAsync(P(lay.chain), 0, lay.chain_bytes, st) != cudaSuccess)
-    return record_cuda_error();
 
   const bool fused_head = use_fused_head(m);
   if (io.stage != kKvOnly) {
@@ -517,63 +347,10 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     return attention_dispatch(a, st);
   };
   const int64_t Hm = m->mlp_hidden;
-  if (chains) {
-    // 6-7 as chained GEMM launches: the linears between two attentions
-    // (out_proj + LN, mlp.0, mlp.2 + the next block's LN, the next qkv) run
-    // row block by row block in one launch each.
-    LinQueue q(m, BL, reinterpret_cast<uint8_t*>(P(lay.chain)), lay.chain_stride, max_chains(m),
-               st);
-    CK_TRY(q.add(chain_link(CK_CHAIN_RESID_LN, P(lay.att), D, D, m->cross_out.w, P(lay.lat),
-                            m->latents, D, L, P(lay.x), m->blocks[0].norm_attn_w,
-                            m->blocks[0].norm_attn_b),
-                 m->cross_out));
-    CK_TRY(q.add(chain_link(CK_CHAIN_STORE, P(lay.x), D, 3 * D, m->blocks[0].qkv.w, P(lay.qkv)),
-                 m->blocks[0].qkv));
-    for (int i = 0; i < m->num_layers; ++i) {
-      const ck_block_weights& w = m->blocks[i];
-      CK_TRY(q.flush());
-      CK_TRY(self_attention());
-      CK_TRY(q.add(chain_link(CK_CHAIN_RESID_LN, P(lay.att), D, D, w.out.w, P(lay.lat), P(lay.lat),
-                              D, 0, P(lay.x), w.norm_mlp_w, w.norm_mlp_b),
-                   w.out));
-      CK_TRY(q.add(chain_link(CK_CHAIN_GELU, P(lay.x), D, Hm, w.mlp0.w, P(lay.hbuf)), w.mlp0));
-      if (i + 1 < m->num_layers) {
-        const ck_block_weights& nx = m->blocks[i + 1];
-        CK_TRY(q.add(chain_link(CK_CHAIN_RESID_LN, P(lay.hbuf), Hm, D, w.mlp2.w, P(lay.lat),
-                                P(lay.lat), D, 0, P(lay.x), nx.norm_attn_w, nx.norm_attn_b),
-                     w.mlp2));
-        CK_TRY(q.add(chain_link(CK_CHAIN_STORE, P(lay.x), D, 3 * D, nx.qkv.w, P(lay.qkv)), nx.qkv));
-      } else {
-        CK_TRY(q.add(chain_link(CK_CHAIN_RESID, P(lay.hbuf), Hm, D, w.mlp2.w, P(lay.lat),
-                                P(lay.lat), D, 0),
-                     w.mlp2));
-      }
-    }
-    CK_TRY(q.flush());
-  } else {
-    // Which norms fold into their linears: a folded consumer needs its producer
-    // (the residual GEMM before it) on the tensor-core path to emit statistics.
-    void* stats = P(lay.stats);
-    auto fold_qkv = [&](int i) {
-      if (i >= m->num_layers) return false;
-      const bool prod = i == 0 ? resid_tc_ok(m, m->cross_out, BL, D, D, P(lay.att), m->latents, D,
-                                             P(lay.lat))
-                               : resid_tc_ok(m, m->blocks[i - 1].mlp2, BL, Hm, D, P(lay.hbuf),
-                                             P(lay.lat), D, P(lay.lat));
-      return prod && fold_tc_ok(m, m->blocks[i].qkv_fold, m->blocks[i].qkv, BL, D, 3 * D, P(lay.lat),
-                                CK_EPI_STORE, P(lay.qkv));
-    };
-    auto fold_mlp0 = [&](int i) {
-      return resid_tc_ok(m, m->blocks[i].out, BL, D, D, P(lay.att), P(lay.lat), D, P(lay.lat)) &&
-             fold_tc_ok(m, m->blocks[i].mlp0_fold, m->blocks[i].mlp0, BL, D, Hm, P(lay.lat),
-                        CK_EPI_GELU, P(lay.hbuf));
-    };
+  {
     // 6. out_proj + broadcast latent residual (and block 0's norm_attn of it)
     bool x_ready = false;  // lay.x already holds norm_attn(lat) for the next block
-    if (fold_qkv(0)) {
-      CK_TRY(lin_stats(m, P(lay.att), BL, D, m->cross_out, D, m->latents, D, L, P(lay.lat), stats,
-                       st));
-    } else if (m->num_layers > 0) {
+    if (m->num_layers > 0) {
       CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, m->cross_out, D, m->latents, D, L, P(lay.lat),
                           m->blocks[0].norm_attn_w, m->blocks[0].norm_attn_b, P(lay.x), st));
       x_ready = true;
@@ -584,29 +361,18 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     // 7. self-attention blocks
     for (int i = 0; i < m->num_layers; ++i) {
       const ck_block_weights& w = m->blocks[i];
-      if (fold_qkv(i)) {
-        CK_TRY(lin_folded(P(lay.lat), BL, D, w.qkv_fold, 3 * D, CK_EPI_STORE, stats, P(lay.qkv), st));
-      } else {
-        if (!x_ready)
-          CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b,
-                          kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
-        CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
-                   3 * D, st));
-      }
+      if (!x_ready)
+        CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b,
+                        kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
+      CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
+                 3 * D, st));
       x_ready = false;
       CK_TRY(self_attention());
-      if (fold_mlp0(i)) {
-        CK_TRY(lin_stats(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat), stats, st));
-        CK_TRY(lin_folded(P(lay.lat), BL, D, w.mlp0_fold, Hm, CK_EPI_GELU, stats, P(lay.hbuf), st));
-      } else {
-        CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat),
-                            w.norm_mlp_w, w.norm_mlp_b, P(lay.x), st));
-        CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, Hm, CK_EPI_GELU, nullptr, 0, 0, P(lay.hbuf), Hm,
-                   st));
-      }
-      if (fold_qkv(i + 1)) {
-        CK_TRY(lin_stats(m, P(lay.hbuf), BL, Hm, w.mlp2, D, P(lay.lat), D, 0, P(lay.lat), stats, st));
-      } else if (i + 1 < m->num_layers) {
+      CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat),
+                          w.norm_mlp_w, w.norm_mlp_b, P(lay.x), st));
+      CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, Hm, CK_EPI_GELU, nullptr, 0, 0, P(lay.hbuf), Hm,
+                 st));
+      if (i + 1 < m->num_layers) {
         CK_TRY(lin_resid_ln(m, P(lay.hbuf), BL, Hm, w.mlp2, D, P(lay.lat), D, 0, P(lay.lat),
                             m->blocks[i + 1].norm_attn_w, m->blocks[i + 1].norm_attn_b, P(lay.x),
                             st));

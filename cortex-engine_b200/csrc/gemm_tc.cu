@@ -15,10 +15,9 @@
 //                quarter, each taking a quarter (half) of the tile's columns in
 //                32-column chunks: tcgen05.ld of the fp32
 //                accumulator (the next chunk's read and residual load in flight
-//                while the current one is finished), the epilogue op (folded
-//                norm, scale, bf16 rounding, GELU / residual / bias, row
-//                statistics), a 64B-swizzled 32 x 32 smem box per chunk and
-//                one TMA tile store per chunk
+//                while the current one is finished), the epilogue op (scale,
+//                bf16 rounding, GELU / residual / bias), a 64B-swizzled
+//                32 x 32 smem box per chunk and one TMA tile store per chunk
 //   warps 18..21 (int8 only: 10..13) int8 -> bf16 converter
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1. All mbarrier waits are bounded
@@ -88,15 +87,12 @@ struct GemmCfg {
   // FUSE_LN: per accumulator buffer, the (mean, M2) partials of the 4 column
   // quarters (2 CTAs x 2 warp column slices) of every row
   static constexpr int XCH_SMEM = LN ? 2 * (2 * EPI_GROUPS) * BM * 8 : 0;
-  // folded LayerNorm: (colsum, bias) of each epilogue warp's BN / 2 columns,
-  // one buffer per TMEM accumulator, so the epilogue reads them at smem latency
-  static constexpr int FOLD_SMEM = FUSE == 1 ? EPI_WARPS * 2 * EPI_COLS * 8 : 0;
   // FUSE_LN: each epilogue warp's gamma | beta columns (bf16), staged once
   // (two warps per lane quarter only: with four, the pipeline ring needs the room
   // and the norm pass reads them through the read-only cache)
   static constexpr int GB_SMEM = (LN && EPI_WARPS == 8) ? EPI_WARPS * 2 * EPI_COLS * 2 : 0;
   static constexpr int BUDGET =
-      232448 - 1024 - BAR_BYTES - EPI_SMEM - FOLD_SMEM - XCH_SMEM - GB_SMEM;
+      232448 - 1024 - BAR_BYTES - EPI_SMEM - XCH_SMEM - GB_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   // bytes completing one stage's barrier (PAIR: both CTAs' loads, on the even CTA's)
   static constexpr int TX_BYTES = (PAIR ? 2 : 1) * (A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES));
@@ -104,7 +100,7 @@ struct GemmCfg {
   static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + EPI_SMEM + FOLD_SMEM + XCH_SMEM + GB_SMEM + BAR_BYTES;
+      1024 + STAGES * STAGE_BYTES + EPI_SMEM + XCH_SMEM + GB_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
   static constexpr uint32_t IDESC_HALF = idesc_bf16(BM, BN / 2, 0u);  // split tiles (NK only)
   static constexpr uint32_t IDESC_PAIR = idesc_bf16(2 * BM, BN, 0u);   // PAIR (NK only)
@@ -124,8 +120,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint8_t* sB = sA + C::STAGES * C::A_BYTES;
   uint8_t* sB8 = sB + C::STAGES * C::B_BYTES;
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
-  float2* sFold = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);  // [8][2][BN/2] (FUSE_NORM)
-  float2* sXch = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(sFold) + C::FOLD_SMEM);
+  float2* sXch = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);
   uint8_t* sGB = reinterpret_cast<uint8_t*>(sXch) + C::XCH_SMEM;  // [EPI_WARPS][gamma | beta]
   uint8_t* sBar = sGB + C::GB_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
@@ -370,28 +365,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     uint8_t* stg = sStg + e * C::STG_WARP;
     int acc = 0;
     uint32_t acc_phase = 0;
-    // Folded LayerNorm (FUSE_NORM): the next tile's row statistics and column
-    // terms are fetched while the current tile is processed (registers for the
-    // statistics, this warp's sFold[e][acc ^ 1] for its columns), so their
-    // global latency stays off the per-tile chain. Warp-private: no barrier.
-    constexpr int FPL = COLS / 32;         // fold columns per lane
-    float2* wfold = sFold + e * 2 * COLS;  // [2][COLS]
-    gemm::StatsRow srow;
-    float2 fold_next[FPL];
-    auto fetch_fold = [&](int t) {
-#pragma unroll
-      for (int j = 0; j < FPL; ++j) {
-        const int n = (t / p.num_m_tiles) * BN + half * COLS + j * 32 + lane;
-        fold_next[j] = n < p.N ? make_float2(__ldg(p.fold_cs + n), __ldg(p.fold_bw + n))
-                               : make_float2(0.f, 0.f);
-      }
-    };
-    if (FUSE == gemm::FUSE_NORM && (int)blockIdx.x < num_tiles) {
-      srow = gemm::load_stats(p, (blockIdx.x % p.num_m_tiles) * BM + row);
-      fetch_fold(blockIdx.x);
-#pragma unroll
-      for (int j = 0; j < FPL; ++j) wfold[j * 32 + lane] = fold_next[j];
-    }
     // FUSE_LN: this warp's gamma | beta columns into shared memory (a CTA
     // keeps one column half: tiles alternate halves and the stride is even),
     // and the residual tile of each row block by TMA into the warp's boxes,
@@ -434,16 +407,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     for (int tile = tile0; tile < num_tiles; tile += tstep) {
       int mt, nt, part;
       tile_mn(tile, mt, nt, part);
-      float nmean = 0.f, nrstd = 0.f;  // folded LayerNorm of this row (FUSE_NORM)
-      if (FUSE == gemm::FUSE_NORM) {
-        gemm::combine_stats(p, srow, nmean, nrstd);
-        __syncwarp();  // this tile's fold terms are in wfold[acc]
-        const int tn = tile + gridDim.x;
-        if (tn < num_tiles) {
-          srow = gemm::load_stats(p, (tn % p.num_m_tiles) * BM + row);
-          fetch_fold(tn);
-        }
-      }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
       if (res_box) {
         if (!mbar_wait(&rbar[e], rph, abort_flag, 10)) break;
@@ -453,8 +416,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
       __syncwarp();
       tc_fence_after();
       const int m = mt * BM + row;
-      float st_shift = 0.f, st_s1 = 0.f, st_s2 = 0.f;  // segment statistics (FUSE_STATS)
-      int st_cnt = 0;
+      float st_shift = 0.f, st_s1 = 0.f, st_s2 = 0.f;  // row statistics (FUSE_LN)
       // a split tile's BN/2 columns are spread over all column slices
       const int col0 = part >= 0 ? half * (COLS / 2) : half * COLS;
       const int nch = part >= 0 ? NCH / 2 : NCH;
@@ -519,11 +481,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
                                                         ((q ^ ((lane >> 1) & 3)) << 4));
           }
           uint32_t packed[16];
-          epilogue_math<EPI, FUSE>(p, m, n0, cur, nmean, nrstd, wfold + acc * COLS + c * 32,
-                                   ((kPrefetch || res_box) && n0 + 32 <= p.N) ? rcur : nullptr,
-                                   packed);
+          epilogue_math<EPI>(p, m, n0, cur,
+                             ((kPrefetch || res_box) && n0 + 32 <= p.N) ? rcur : nullptr, packed);
           if (C::LN) tmem_st16w(tbase + (uint32_t)(c * 32), packed);  // Y, for the norm pass
-          if (FUSE == gemm::FUSE_STATS || C::LN) {
+          if (C::LN) {
             // statistics of the values as stored (bf16), shifted by the
             // segment's first value so the sum of squares does not cancel
 #pragma unroll
@@ -545,7 +506,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
             }
             st_s1 += s1a + s1b;
             st_s2 += s2a + s2b;
-            st_cnt += min(32, p.N - n0);
           }
           // 64B-swizzled 32 x 32 box, then one TMA store per chunk; the box was
           // last read by the store issued two chunks ago
@@ -574,16 +534,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           }
         }
         if (kAhead && c + 1 < nch) tc_wait_ld();
-      }
-      if (FUSE == gemm::FUSE_NORM && tile + (int)gridDim.x < num_tiles) {
-#pragma unroll
-        for (int j = 0; j < FPL; ++j) wfold[(acc ^ 1) * COLS + j * 32 + lane] = fold_next[j];
-      }
-      if (FUSE == gemm::FUSE_STATS && m < p.M && st_cnt > 0) {
-        const int seg = (nt * BN + col0) / p.stats_sw;
-        const float mu = st_s1 / (float)st_cnt;
-        p.stats_out[(int64_t)seg * p.M + m] =
-            make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
       }
       if constexpr (C::LN) {
         // the first pass's boxes (Y) go out together
@@ -774,9 +724,6 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   return finish_launch(cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, ty2, tr, a));
 }
 
-// Instantiated combinations: a folded LayerNorm feeds only bf16 (N, K) weights
-// with a store or GELU epilogue; statistics come only from bf16 residual
-// epilogues.
 // (dispatch value for a 2-SM pair launch, beside the gemm::Fuse modes)
 constexpr int FUSE_PAIR = 100;
 
@@ -786,8 +733,6 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
                  const GemmArgs& a, cudaStream_t st) {
   using gemm::FUSE_LN;
   using gemm::FUSE_NONE;
-  using gemm::FUSE_NORM;
-  using gemm::FUSE_STATS;
   // every instantiation takes the second output map; only FUSE_LN writes it
   if (fuse == FUSE_PAIR) {
     if constexpr (BN == 256 && WMODE == W_BF16_NK) {
@@ -799,19 +744,6 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
   if (fuse == FUSE_LN) {
     if constexpr (BN == 256) {
       if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_LN>(ta, tb, ty0, ty2, tr, a, st);
-    }
-    return CK_ERR_UNSUPPORTED;
-  }
-  if (fuse == FUSE_NORM) {
-    if constexpr (WMODE == W_BF16_NK) {
-      if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NORM>(ta, tb, ty0, ty2, tr, a, st);
-      if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NORM>(ta, tb, ty0, ty2, tr, a, st);
-    }
-    return CK_ERR_UNSUPPORTED;
-  }
-  if (fuse == FUSE_STATS) {
-    if constexpr (WMODE != W_I8_NK) {
-      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_STATS>(ta, tb, ty0, ty2, tr, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
@@ -865,12 +797,6 @@ bool gemm_split_enabled() {
 
 int gemm_tc_block_n(int64_t N) { return (N % 256 == 0 || N > 256) ? 256 : 128; }
 
-int gemm_tc_stats_width(int64_t N, int w_dtype) {
-  const int BN = gemm_tc_block_n(N);
-  return w_dtype == CK_I8 ? BN / GemmCfg<256, W_I8_NK, 2, CK_EPI_RESID>::EPI_GROUPS
-                          : BN / GemmCfg<256, W_BF16_NK, 2, CK_EPI_RESID>::EPI_GROUPS;
-}
-
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
             int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st,
@@ -891,14 +817,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.w_scale = (w_dtype == CK_I8) ? w_scale : nullptr;
   if (w_dtype == CK_I8 && w_scale == nullptr) return CK_ERR_INVALID_ARG;
   a.scale_vec = (reinterpret_cast<uintptr_t>(w_scale) & 15u) == 0;
-  a.stats_out = nullptr;
-  a.stats_sw = gemm_tc_stats_width(N, w_dtype);
-  a.stats_in = nullptr;
-  a.stats_in_sw = 0;
-  a.stats_in_nseg = 0;
   a.norm_eps = 0.f;
-  a.fold_cs = nullptr;
-  a.fold_bw = nullptr;
   a.ln_gamma = nullptr;
   a.ln_beta = nullptr;
   a.res_tma = 0;
@@ -918,24 +837,6 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     a.ln_beta = reinterpret_cast<const __nv_bfloat16*>(fz->ln_beta);
     a.norm_eps = fz->eps;
     fuse = gemm::FUSE_LN;
-  } else if (fz != nullptr && fz->stats_out != nullptr) {
-    if (epi != CK_EPI_RESID) return CK_ERR_UNSUPPORTED;
-    a.stats_out = reinterpret_cast<float2*>(fz->stats_out);
-    fuse = gemm::FUSE_STATS;
-  } else if (fz != nullptr && fz->stats_in != nullptr) {
-    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-    if (w_dtype != CK_BF16 || w_layout != CK_W_NK || (epi != CK_EPI_STORE && epi != CK_EPI_GELU) ||
-        fz->stats_in_sw <= 0 || fz->fold_cs == nullptr || fz->fold_bw == nullptr ||
-        !al16(fz->fold_cs) || !al16(fz->fold_bw))
-      return CK_ERR_UNSUPPORTED;
-    a.stats_in = reinterpret_cast<const float2*>(fz->stats_in);
-    a.stats_in_sw = fz->stats_in_sw;
-    a.stats_in_nseg = (int)((K + fz->stats_in_sw - 1) / fz->stats_in_sw);
-    if (a.stats_in_nseg > 8) return CK_ERR_UNSUPPORTED;
-    a.norm_eps = fz->eps;
-    a.fold_cs = fz->fold_cs;
-    a.fold_bw = fz->fold_bw;
-    fuse = gemm::FUSE_NORM;
   }
 
   // 2-SM pairs (256-row tiles, B split over the pair): bf16 (N, K) weights, a

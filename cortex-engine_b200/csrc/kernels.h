@@ -45,21 +45,11 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
 bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_layout, int64_t N,
                        int64_t ldw, const void* A, const void* W, int64_t ldy, const void* Y,
                        int epi, const void* aux, int64_t ld_aux);
-// Optional epilogue fusions of the tcgen05 GEMM (see gemm_common.cuh):
-//   stats_out  residual epilogue also writes per-row, per-segment (mean, M2)
-//              of its output, segment width gemm_tc_stats_width(N, w_dtype)
-//   stats_in   LayerNorm folded into this GEMM: A is the raw residual, W is
-//              W * gamma, fold_cs[n] = sum_k W[n,k] * gamma[k] (as stored),
-//              fold_bw[n] = sum_k W[n,k] * beta[k]
+// Optional epilogue fusion of the tcgen05 GEMM (see gemm_common.cuh):
 //   ln_out     residual epilogue also writes LayerNorm(Y) (gamma ln_gamma, beta
 //              ln_beta or none, eps) to ln_out (row stride ln_ld): bf16, N = 512
 struct GemmFusion {
-  void* stats_out;
-  const void* stats_in;
-  int stats_in_sw;
-  float eps;
-  const float* fold_cs;
-  const float* fold_bw;
+  float eps = 0.f;
   void* ln_out = nullptr;
   int64_t ln_ld = 0;
   const void* ln_gamma = nullptr;
@@ -78,41 +68,10 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
                     int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
                     int64_t ldy, cudaStream_t st, bool w_static = false);
 int gemm_tc_block_n(int64_t N);
-int gemm_tc_stats_width(int64_t N, int w_dtype);  // column width of one statistics segment
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,
             int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy, cudaStream_t st,
             const GemmFusion* fz = nullptr);
-
-// Chained tcgen05 GEMMs (gemm_chain.cu): up to four bf16 linears in one
-// launch, linear i reading linear i-1's output (Y, or Y2 of a LayerNorm
-// linear) as A, row block by row block. Weights are (N, K) bf16 with row
-// stride K, N a multiple of 512; a RESID_LN linear has N = 512 and also
-// writes LayerNorm(Y) to Y2. aux_link names the earlier linear of the chain
-// that writes a residual linear's aux (-1: written before the launch).
-// counters: gemm_chain_counter_bytes of zeroed device memory per launch.
-enum { CK_CHAIN_STORE = 0, CK_CHAIN_GELU = 1, CK_CHAIN_RESID = 2, CK_CHAIN_RESID_LN = 3 };
-struct ChainLinear {
-  int kind;
-  const void* A;
-  int64_t lda;
-  const void* W;
-  int64_t N, K;
-  const void* aux;
-  int64_t ld_aux, aux_row_mod;
-  int aux_link;
-  void* Y;
-  int64_t ldy;
-  void* Y2;
-  int64_t ldy2;
-  const void* ln_gamma;
-  const void* ln_beta;
-  float eps;
-};
-bool gemm_chain_enabled();  // CK_CHAIN=1 in the environment turns chains on
-bool gemm_chain_supported(const ChainLinear* l, int n_links, int64_t M);
-size_t gemm_chain_counter_bytes(int64_t M, int n_links);
-int gemm_chain(const ChainLinear* l, int n_links, int64_t M, int* counters, cudaStream_t st);
 
 // CUDA-core GEMM, fp32 accumulate (gemm_simt.cu)
 int gemm_simt(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const void* W,

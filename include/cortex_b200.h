@@ -191,25 +191,11 @@ typedef struct ck_linear_weight {
   const void* bias;    /* (N,) or NULL */
 } ck_linear_weight;
 
-/* A LayerNorm folded into the linear that consumes it (ck_norm_fold_weights):
- *   LN(x) W^T = rstd * (x (W*gamma)^T - mean * colsum) + bias
- * w = W * gamma along K (bf16, (N, K)), colsum[n] = sum_k w[n, k], bias[n] =
- * sum_k W[n, k] * beta[k]. With w set, ck_forward feeds the raw residual rows
- * to the GEMM and applies the norm in its epilogue, from row statistics that
- * the preceding residual GEMM emits; no normalised copy is written. */
-typedef struct ck_norm_fold {
-  const void* w;
-  const float* colsum;
-  const float* bias;
-} ck_norm_fold;
-
 typedef struct ck_block_weights {
   const void *norm_attn_w, *norm_attn_b;
   ck_linear_weight qkv, out;
   const void *norm_mlp_w, *norm_mlp_b;
   ck_linear_weight mlp0, mlp2;
-  ck_norm_fold qkv_fold;  /* norm_attn folded into qkv; w == NULL: not folded */
-  ck_norm_fold mlp0_fold; /* norm_mlp folded into mlp.0;  w == NULL: not folded */
 } ck_block_weights;
 
 typedef struct ck_model {
@@ -227,14 +213,6 @@ typedef struct ck_model {
   const void *head_norm_w, *head_norm_b;
   ck_linear_weight head_q, head_kv, head_out;
 } ck_model;
-
-/* Builds a ck_norm_fold for a bf16 (N, K) weight W (row stride ldw) and a
- * LayerNorm (gamma, beta: (K,) bf16; beta may be NULL): writes w_out (N, K)
- * bf16 contiguous, colsum (N,) and bias (N,) fp32. Weight preparation, run once
- * per weight update; no reference counterpart (the reference normalises x). */
-int ck_norm_fold_weights(const void* W, int64_t N, int64_t K, int64_t ldw, const void* gamma,
-                         const void* beta, void* w_out, float* colsum, float* bias,
-                         void* stream);
 
 size_t ck_forward_workspace_bytes(const ck_model* m, int64_t E, int32_t B);
 int ck_forward(const ck_model* m, const void* neuron_ids, const void* time_bins,

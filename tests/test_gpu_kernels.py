@@ -456,29 +456,3 @@ def test_attention_temporal_mask():
     ref = O.sparse_cross_attention(q.float(), k.float(), v.float(), mask, 64, 64)
     out = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask, 64, 64)
     torch.testing.assert_close(out.float().cpu(), ref, rtol=1e-2, atol=1e-2)
-
-
-@pytest.mark.parametrize("N,K,beta", [(1536, 512, True), (2048, 768, True), (40, 64, False)])
-def test_norm_fold_weights(N, K, beta):
-    """ck_norm_fold_weights: w = bf16(W * gamma), colsum = sum_k w, bias = W @ beta."""
-    from cortex import _lib as L
-
-    g = torch.Generator(device="cpu").manual_seed(N + K)
-    W = (torch.randn(N, K, generator=g) / K ** 0.5).to(torch.bfloat16)
-    gamma = (1 + 0.3 * torch.randn(K, generator=g)).to(torch.bfloat16)
-    b = (0.2 * torch.randn(K, generator=g)).to(torch.bfloat16) if beta else None
-    Wd, gd = W.to(DEV), gamma.to(DEV)
-    bd = b.to(DEV) if beta else None
-    wf = torch.empty(N, K, dtype=torch.bfloat16, device=DEV)
-    cs = torch.empty(N, dtype=torch.float32, device=DEV)
-    bw = torch.empty(N, dtype=torch.float32, device=DEV)
-    rc = L.load().ck_norm_fold_weights(Wd.data_ptr(), N, K, K, gd.data_ptr(),
-                                       bd.data_ptr() if beta else None, wf.data_ptr(),
-                                       cs.data_ptr(), bw.data_ptr(), L.stream_of(Wd.device))
-    L.check(rc, "ck_norm_fold_weights")
-    torch.cuda.synchronize()
-    exp_w = (W.float() * gamma.float()).to(torch.bfloat16)
-    assert torch.equal(wf.cpu(), exp_w)
-    torch.testing.assert_close(cs.cpu(), exp_w.double().sum(1).float(), rtol=1e-5, atol=1e-4)
-    exp_b = (W.double() @ b.double()).float() if beta else torch.zeros(N)
-    torch.testing.assert_close(bw.cpu(), exp_b, rtol=1e-5, atol=1e-4)

@@ -198,36 +198,6 @@ def test_fused_head_matches_composed_head(monkeypatch, name, latents, layers):
 
 
 @pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
-def test_norm_fold_matches_separate_norms(monkeypatch, name):
-    """LayerNorms folded into qkv_proj / mlp.0 (raw residual into the GEMM,
-    statistics from the producing residual epilogue) against separate norm
-    kernels and the oracle. cfg2 keeps its INT8 qkv / mlp.0 unfolded while the
-    INT8 residual GEMMs still run; cfg3 is ragged."""
-    from cortex.workloads import make_inputs
-
-    wl, model = _model(name)
-    with torch.no_grad():  # non-trivial affine parameters, so the fold is exercised
-        g = torch.Generator(device="cpu").manual_seed(5)
-        for blk in model.encoder.self_attn_blocks:
-            for nrm in (blk.norm_attn, blk.norm_mlp):
-                nrm.weight.copy_(1 + 0.2 * torch.randn(nrm.weight.shape, generator=g))
-                nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
-    inp, _ = make_inputs(wl, seed=6, batch=8)
-    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    with torch.no_grad():  # device indices: the eager path reads the switch every call
-        monkeypatch.setenv("CK_NORM_FOLD", "1")
-        folded = model(*(inp[k].to(DEV) for k in cols))["behavior"]
-        monkeypatch.setenv("CK_NORM_FOLD", "0")
-        separate = model(*(inp[k].to(DEV) for k in cols))["behavior"]
-    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
-           for k, v in model.state_dict().items()}
-    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
-    assert torch.isfinite(folded).all()
-    assert _rel(folded, separate) <= 1e-2, _rel(folded, separate)
-    assert _rel(folded, ref) <= TOL["bfloat16"], _rel(folded, ref)
-
-
-@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
 def test_layernorm_fused_into_residual_gemm(monkeypatch, name):
     """Each LayerNorm after a residual GEMM with D = 512 is the GEMM's second
     output (a CTA pair per row block exchanging row statistics through
@@ -245,7 +215,7 @@ def test_layernorm_fused_into_residual_gemm(monkeypatch, name):
                 nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
     inp, _ = make_inputs(wl, seed=9, batch=None if name == "cfg3" else 8)
     cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    monkeypatch.setenv("CK_CHAIN", "0")  # one launch per linear: the GEMM's own LayerNorm
+
     with torch.no_grad():
         monkeypatch.setenv("CK_LN_FUSE", "1")
         fused, n_fused = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
@@ -265,81 +235,6 @@ def test_layernorm_fused_into_residual_gemm(monkeypatch, name):
            for k, v in model.state_dict().items()}
     ref = O.forward(p32, wl.config, *(torch.from_numpy(sub[k]) for k in cols)).float()
     assert _rel(fused[:n], ref) <= TOL["bfloat16"], _rel(fused[:n], ref)
-
-
-@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
-def test_chained_gemms_match_separate_launches(monkeypatch, name):
-    """The linears between two attentions (out_proj + LayerNorm, mlp.0, mlp.2 +
-    the next block's LayerNorm, the next qkv_proj) as one chained launch, with
-    row-block counters between the linears and the LayerNorm row statistics
-    exchanged inside a CTA pair, against one launch per linear and the oracle.
-    cfg2's block linears are all INT8, which chains do not take: it runs the
-    same launches either way. cfg3 (B=256, ragged events) gives every cluster
-    several jobs per linear."""
-    from cortex.sharding import slice_events
-    from cortex.workloads import make_inputs
-
-    wl, model = _model(name)
-    with torch.no_grad():
-        g = torch.Generator(device="cpu").manual_seed(12)
-        for blk in model.encoder.self_attn_blocks:
-            for nrm in (blk.norm_attn, blk.norm_mlp):
-                nrm.weight.copy_(1 + 0.2 * torch.randn(nrm.weight.shape, generator=g))
-                nrm.bias.copy_(0.1 * torch.randn(nrm.bias.shape, generator=g))
-    inp, _ = make_inputs(wl, seed=13, batch=None if name == "cfg3" else 8)
-    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    with torch.no_grad():  # device indices: the eager path reads the switch every call
-        monkeypatch.setenv("CK_CHAIN", "1")
-        chained, n_chain = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
-        again = model(*(inp[k].to(DEV) for k in cols))["behavior"]
-        monkeypatch.setenv("CK_CHAIN", "0")
-        separate, n_sep = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
-    layers = wl.config.num_layers
-    assert torch.isfinite(chained).all()
-    assert torch.equal(chained, again)  # deterministic
-    # bf16: 2 + 4 L - 1 linears in L + 1 chains
-    assert n_sep - n_chain == (0 if wl.int8 else 3 * layers), (n_sep, n_chain)
-    if wl.int8:
-        assert torch.equal(chained, separate)
-    assert _rel(chained, separate) <= 1e-2, _rel(chained, separate)
-    n = 16 if name == "cfg3" else chained.shape[0]  # oracle on a subset (windows are independent)
-    sub = slice_events({k: inp[k].numpy() for k in cols},
-                       np.bincount(inp["batch_indices"].numpy()), 0, n)
-    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
-           for k, v in model.state_dict().items()}
-    ref = O.forward(p32, wl.config, *(torch.from_numpy(sub[k]) for k in cols)).float()
-    assert _rel(chained[:n], ref) <= TOL["bfloat16"], _rel(chained[:n], ref)
-
-
-@pytest.mark.parametrize("latents,batch", [(64, 3), (200, 5), (1000, 2)])
-def test_chained_gemms_ragged_row_blocks(monkeypatch, latents, batch):
-    """Chains whose row count B * L is not a multiple of the 128-row tile (the
-    last row block is partial: TMA clips its stores, its counters still count
-    every epilogue warp) and chains with fewer jobs than clusters."""
-    import dataclasses
-
-    from cortex.workloads import WORKLOADS, build_model, make_inputs
-
-    wl = WORKLOADS["cfg1"]
-    wl = dataclasses.replace(wl, config=wl.config.model_copy(update={"num_latents": latents,
-                                                                     "num_layers": 2}))
-    model = build_model(wl, DEV)
-    inp, _ = make_inputs(wl, seed=14, batch=batch)
-    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    with torch.no_grad():
-        monkeypatch.setenv("CK_CHAIN", "1")
-        chained, n_chain = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
-        monkeypatch.setenv("CK_CHAIN", "0")
-        separate, n_sep = _launches(lambda: model(*(inp[k].to(DEV) for k in cols))["behavior"])
-    # 2 + 4 L - 1 linears in L + 1 chains; with a latent count that is not a
-    # multiple of 32 the separate path also keeps the cross LayerNorm apart
-    # (its broadcast residual does not come in 32-row boxes)
-    assert n_sep - n_chain == 6 + (1 if latents % 32 else 0), (n_sep, n_chain)
-    assert _rel(chained, separate) <= 1e-2, _rel(chained, separate)
-    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
-           for k, v in model.state_dict().items()}
-    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
-    assert _rel(chained, ref) <= TOL["bfloat16"], _rel(chained, ref)
 
 
 def test_side_stream_prologue_is_bit_identical_and_per_thread(monkeypatch):
@@ -377,23 +272,3 @@ def test_side_stream_prologue_is_bit_identical_and_per_thread(monkeypatch):
     assert torch.equal(forked, single)
     assert len(results) == 3 and all(torch.equal(y, single) for y in results)
 
-
-def test_norm_fold_follows_inplace_parameter_updates(monkeypatch):
-    """The folded weights are derived data: an in-place update of a norm or a
-    linear weight (version counter) rebuilds them before the next forward."""
-    from cortex.workloads import make_inputs
-
-    monkeypatch.setenv("CK_NORM_FOLD", "1")
-    wl, model = _model("cfg1")
-    inp, _ = make_inputs(wl, seed=7, batch=4)
-    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
-    with torch.no_grad():
-        before = model(*(inp[k] for k in cols))["behavior"]
-        model.encoder.self_attn_blocks[0].norm_attn.weight.mul_(1.7)
-        model.encoder.self_attn_blocks[2].mlp[0].weight.mul_(0.5)
-        after = model(*(inp[k] for k in cols))["behavior"]
-    p32 = {k: (v.float() if v.is_floating_point() else v).cpu()
-           for k, v in model.state_dict().items()}
-    ref = O.forward(p32, wl.config, *(inp[k] for k in cols)).float()
-    assert not torch.equal(before, after)
-    assert _rel(after, ref) <= TOL["bfloat16"], _rel(after, ref)
