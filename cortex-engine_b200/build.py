@@ -42,6 +42,7 @@ SOURCES = [
     "ingest.cu",
     "rows.cu",
     "runner.cpp",
+    "trace.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -90,12 +90,18 @@ class Model(ctypes.Structure):
     ]
 
 
+class TraceRecord(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 96), ("stream", _vp), ("ms", _f32)]
+
+
 _SIGS = {
     "ck_get_last_status": (_int, [ctypes.POINTER(_int)]),
     "ck_last_cuda_error": (_int, []),
     "ck_status_string": (ctypes.c_char_p, [_int]),
     "ck_num_sms": (_int, []),
     "ck_launch_count": (ctypes.c_longlong, []),
+    "ck_trace_begin": (_int, [_i32]),
+    "ck_trace_end": (_int, [ctypes.POINTER(TraceRecord), _i32, ctypes.POINTER(_i32)]),
     "ck_pack_workspace_bytes": (_sz, [_i64, _i32]),
     "ck_pack_events": (_int, [_vp, _int, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ck_pack_scatter": (_int, [_vp, _int, _i64, _i32, _i64, _vp, _int, _i64, _vp, _vp, _i32,

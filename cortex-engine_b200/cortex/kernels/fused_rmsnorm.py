@@ -2,11 +2,13 @@
 
 ``rms_norm_linear(x, gamma, w, bias=None, eps=1e-6)`` keeps the reference
 signature (cortex/kernels/fused_rmsnorm.py:239-301): ``x`` is (..., K), ``w`` is
-(K, N), the result (..., N). The norm is computed in fp32 and rounded to the
-input dtype exactly as ``rms_norm_linear_reference`` does (:86-108); the GEMM
-then runs on the tcgen05 kernel for bf16 (``w`` read N-major through TMA, no
-transpose copy) or on the fp32 CUDA-core kernel for fp32 and for shapes whose
-strides TMA cannot take. A bias is added after rounding the product, as the
+(K, N), the result (..., N). For bf16 it is one tcgen05 launch (``w`` read
+N-major through TMA, no transpose copy): the GEMM's norm warps scale each
+TMA-loaded tile of x by gamma in shared memory and sum x^2 per row, and the
+epilogue multiplies each row by 1 / sqrt(mean(x^2) + eps) before the bias.
+fp32 (and shapes whose strides TMA cannot take) normalise in fp32, round to
+the input dtype as ``rms_norm_linear_reference`` does (:86-108), then run the
+fp32 CUDA-core GEMM. A bias is added after rounding the product, as the
 reference's ``out + bias`` does. CUDA tensors only.
 """
 
@@ -51,14 +53,24 @@ def rms_norm_linear(x: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor,
         return out.reshape(*lead, N)
     lib = L.load()
     dt = L.dtype_code(x.dtype)
-    ws_bytes = lib.ck_norm_linear_workspace_bytes(dt, M, K)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     g = gamma.to(x.dtype).contiguous()
     b = bias.to(x.dtype).contiguous() if bias is not None else None
-    rc = lib.ck_norm_linear(L.ptr(x2), dt, M, K, x2.stride(0), L.ptr(g), None, float(eps),
-                            L.CK_NORM_RMS, L.ptr(w), dt, L.CK_W_KN, N, w.stride(0), None,
-                            L.CK_EPI_BIAS if b is not None else L.CK_EPI_STORE, L.ptr(b), 0, 0,
-                            L.ptr(out), out.stride(0), L.ptr(ws), ws_bytes, L.stream_of(dev))
+
+    def call(ws, ws_bytes):
+        return lib.ck_norm_linear(L.ptr(x2), dt, M, K, x2.stride(0), L.ptr(g), None, float(eps),
+                                  L.CK_NORM_RMS, L.ptr(w), dt, L.CK_W_KN, N, w.stride(0), None,
+                                  L.CK_EPI_BIAS if b is not None else L.CK_EPI_STORE, L.ptr(b),
+                                  0, 0, L.ptr(out), out.stride(0), ws, ws_bytes,
+                                  L.stream_of(dev))
+
+    # bf16 rows run as one launch with the norm inside the GEMM and need no
+    # workspace; the library says so (CK_ERR_WORKSPACE, nothing launched) when
+    # a call needs one
+    rc = call(None, 0)
+    if rc == L.CK_ERR_WORKSPACE:
+        ws_bytes = lib.ck_norm_linear_workspace_bytes(dt, M, K)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        rc = call(L.ptr(ws), ws_bytes)
     L.check(rc, "ck_norm_linear")
     return out.reshape(*lead, N)
 

@@ -33,6 +33,48 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
                    aux_row_mod, Y, ldy, st);
 }
 
+bool norm_linear_fused(int dtype, int64_t M, int64_t K, int64_t ldx, const void* x,
+                       const void* gamma, int norm_mode, const void* W, int w_dtype,
+                       int w_layout, int64_t N, int64_t ldw, int epi, const void* aux,
+                       int64_t ld_aux, const void* Y, int64_t ldy) {
+  return norm_mode == CK_NORM_RMS && dtype == CK_BF16 && gamma != nullptr && K <= 4096 &&
+         (epi == CK_EPI_STORE || epi == CK_EPI_BIAS) && (w_dtype == CK_BF16 || w_dtype == CK_I8) &&
+         gemm_tc_supported(M, K, ldx, w_dtype, w_layout, N, ldw, x, W, ldy, Y, epi, aux, ld_aux);
+}
+
+int norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* gamma,
+                const void* beta, float eps, int norm_mode, const void* W, int w_dtype,
+                int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi,
+                const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy,
+                void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  if (norm_mode == CK_NORM_NONE)
+    return linear_dispatch(x, dtype, M, K, ldx, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux,
+                           ld_aux, aux_row_mod, Y, ldy, st);
+  if (norm_mode != CK_NORM_LAYER && norm_mode != CK_NORM_RMS) return CK_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K <= 0) return CK_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return CK_OK;
+  if (!x || !gamma || !W || !Y) return CK_ERR_INVALID_ARG;
+  if (epi < CK_EPI_STORE || epi > CK_EPI_BIAS) return CK_ERR_INVALID_ARG;
+  if ((epi == CK_EPI_RESID || epi == CK_EPI_BIAS) && aux == nullptr) return CK_ERR_INVALID_ARG;
+  if (w_dtype == CK_I8 && (w_scale == nullptr || w_layout != CK_W_NK)) return CK_ERR_INVALID_ARG;
+  // RMSNorm with bf16 activations: one launch, the norm inside the tcgen05 GEMM
+  if (norm_linear_fused(dtype, M, K, ldx, x, gamma, norm_mode, W, w_dtype, w_layout, N, ldw, epi,
+                        aux, ld_aux, Y, ldy)) {
+    GemmFusion fz;
+    fz.rms_gamma = gamma;
+    fz.eps = eps;
+    return gemm_tc(x, M, K, ldx, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux, ld_aux,
+                   aux_row_mod, Y, ldy, st, &fz);
+  }
+  // otherwise the normalised rows go through the workspace to a second launch
+  if (workspace == nullptr || workspace_bytes < (size_t)M * (size_t)K * (dtype == CK_F32 ? 4 : 2))
+    return CK_ERR_WORKSPACE;
+  int rc = row_norm(x, dtype, M, (int32_t)K, ldx, gamma, beta, eps, norm_mode, workspace, K, st);
+  if (rc != CK_OK) return rc;
+  return linear_dispatch(workspace, dtype, M, K, K, W, w_dtype, w_layout, N, ldw, w_scale, epi,
+                         aux, ld_aux, aux_row_mod, Y, ldy, st);
+}
+
 int attention_dispatch(const ck_attention_args& a, cudaStream_t st) {
   if (a.B < 0 || a.H <= 0 || a.Dh <= 0 || a.Lq < 0) return CK_ERR_INVALID_ARG;
   if (a.B == 0 || a.Lq == 0) return CK_OK;
@@ -110,17 +152,9 @@ int ck_norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, 
                    int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi,
                    const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy,
                    void* workspace, size_t workspace_bytes, void* stream) {
-  if (norm_mode == CK_NORM_NONE)
-    return linear_dispatch(x, dtype, M, K, ldx, W, w_dtype, w_layout, N, ldw, w_scale, epi, aux,
-                           ld_aux, aux_row_mod, Y, ldy, S(stream));
-  if (M == 0) return CK_OK;
-  if (workspace == nullptr || workspace_bytes < ck_norm_linear_workspace_bytes(dtype, M, K))
-    return CK_ERR_WORKSPACE;
-  int rc = row_norm(x, dtype, M, (int32_t)K, ldx, gamma, beta, eps, norm_mode, workspace, K,
-                    S(stream));
-  if (rc != CK_OK) return rc;
-  return linear_dispatch(workspace, dtype, M, K, K, W, w_dtype, w_layout, N, ldw, w_scale, epi,
-                         aux, ld_aux, aux_row_mod, Y, ldy, S(stream));
+  return norm_linear(x, dtype, M, K, ldx, gamma, beta, eps, norm_mode, W, w_dtype, w_layout, N,
+                     ldw, w_scale, epi, aux, ld_aux, aux_row_mod, Y, ldy, workspace,
+                     workspace_bytes, S(stream));
 }
 
 int ck_attention(const ck_attention_args* args, void* stream) {

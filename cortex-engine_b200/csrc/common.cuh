@@ -166,6 +166,35 @@ __device__ __forceinline__ void rbf2(float& a, float& b) {
   b = bf16_hi(r);
 }
 
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// Four int8 values (one 32-bit word, little-endian) to four bf16 values, exact,
+// on the integer and FMA pipes rather than the conversion unit (I2F and F2F
+// issue at a fraction of the FMA rate; with one I2F per element and one F2F per
+// pair they made the int8 weight tiles the slowest stage of the GEMM pipeline). Each byte, flipped to the unsigned v + 128, is
+// placed in the low byte of the fp32 word 0x4B000000 (2^23, whose last place is
+// 1), so the word holds 2^23 + 128 + v exactly; one paired subtraction leaves v.
+// An fp32 integer of magnitude <= 128 has at most 8 significant bits, so its
+// upper 16 bits are its bf16 value, and one byte permute packs two of them.
+__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t magic = 0x4B000000u;
+  const unsigned long long bias = f2pk(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  float a0, a1, a2, a3;
+  f2up(fadd2(f2pk(__uint_as_float(prmt(u, magic, 0x7540u)), __uint_as_float(prmt(u, magic, 0x7541u))),
+             bias),
+       a0, a1);
+  f2up(fadd2(f2pk(__uint_as_float(prmt(u, magic, 0x7542u)), __uint_as_float(prmt(u, magic, 0x7543u))),
+             bias),
+       a2, a3);
+  lo = prmt(__float_as_uint(a0), __float_as_uint(a1), 0x7632u);
+  hi = prmt(__float_as_uint(a2), __float_as_uint(a3), 0x7632u);
+}
+
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

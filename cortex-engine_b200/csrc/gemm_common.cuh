@@ -30,9 +30,13 @@ struct GemmArgs {
   // ahead of the accumulator, else by per-row loads
   int res_tma;
   int pre_b;  // B (the weight) may be prefetched before the dependency wait
+  // RMSNorm of A fused into the GEMM (FUSE_RMS): the norm warps scale every
+  // A tile by rms_gamma in shared memory and sum x^2 per row; the epilogue
+  // multiplies each row by 1 / sqrt(sum / K + norm_eps).
+  const __nv_bfloat16* rms_gamma;
 };
 
-enum Fuse { FUSE_NONE = 0, FUSE_LN = 3 };
+enum Fuse { FUSE_NONE = 0, FUSE_LN = 3, FUSE_RMS = 4 };
 
 __device__ __forceinline__ int64_t residual_row(const GemmArgs& p, int m) {
   return p.aux_row_mod > 0 ? (m % p.aux_row_mod) : m;

@@ -69,7 +69,8 @@ struct GemmCfg {
   // LayerNorm with bf16 weights, whose two-pass epilogue is latency-bound and
   // lies on the critical path (one tile per CTA); two per quarter otherwise
   // (and always in int8 mode, whose converter warps need the registers)
-  static constexpr bool LN = FUSE == 3;  // gemm::FUSE_LN
+  static constexpr bool LN = FUSE == 3;   // gemm::FUSE_LN
+  static constexpr bool RMS = FUSE == 4;  // gemm::FUSE_RMS
   static constexpr int EPI_WARPS =
       (WMODE != W_I8_NK && (EPI == CK_EPI_GELU || LN)) ? 16 : 8;
   static constexpr int EPI_GROUPS = EPI_WARPS / 4;  // column slices of a tile
@@ -83,7 +84,7 @@ struct GemmCfg {
   // else two (one with four warps per lane quarter)
   static constexpr int STG_WARP = (LN ? EPI_COLS / 32 : (EPI_WARPS == 8 ? 2 : 1)) * STG_BOX;
   static constexpr int EPI_SMEM = EPI_WARPS * STG_WARP;
-  static constexpr int BAR_BYTES = LN ? 512 : 256;
+  static constexpr int BAR_BYTES = (LN || RMS) ? 512 : 256;
   // FUSE_LN: per accumulator buffer, the (mean, M2) partials of the 4 column
   // quarters (2 CTAs x 2 warp column slices) of every row
   static constexpr int XCH_SMEM = LN ? 2 * (2 * EPI_GROUPS) * BM * 8 : 0;
@@ -91,16 +92,26 @@ struct GemmCfg {
   // (two warps per lane quarter only: with four, the pipeline ring needs the room
   // and the norm pass reads them through the read-only cache)
   static constexpr int GB_SMEM = (LN && EPI_WARPS == 8) ? EPI_WARPS * 2 * EPI_COLS * 2 : 0;
-  static constexpr int BUDGET =
-      232448 - 1024 - BAR_BYTES - EPI_SMEM - XCH_SMEM - GB_SMEM;
+  // FUSE_RMS: gamma over all of K (bf16, zero past K), staged once per CTA,
+  // and the per-row 1 / rms of each TMEM accumulator buffer
+  static constexpr int RMS_KMAX = 4096;
+  static constexpr int GAM_SMEM = RMS ? RMS_KMAX * 2 : 0;
+  static constexpr int RSTD_SMEM = RMS ? 2 * BM * 4 : 0;
+  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - XCH_SMEM - GB_SMEM -
+                                GAM_SMEM - RSTD_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   // bytes completing one stage's barrier (PAIR: both CTAs' loads, on the even CTA's)
   static constexpr int TX_BYTES = (PAIR ? 2 : 1) * (A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES));
   static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
-  static constexpr int NUM_THREADS = 32 * (CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0));
+  static constexpr int NORM_WARP0 = CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0);
+  static constexpr int NUM_THREADS = 32 * (NORM_WARP0 + (RMS ? 4 : 0));
+  // arrivals that make a stage's operands ready for the MMA after the TMA:
+  // the int8 converter and / or the RMS norm warpgroup, 128 threads each
+  static constexpr int CONV_COUNT = 128 * ((WMODE == W_I8_NK ? 1 : 0) + (RMS ? 1 : 0));
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + EPI_SMEM + XCH_SMEM + GB_SMEM + BAR_BYTES;
+      1024 + STAGES * STAGE_BYTES + EPI_SMEM + XCH_SMEM + GB_SMEM + GAM_SMEM + RSTD_SMEM +
+      BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
   static constexpr uint32_t IDESC_HALF = idesc_bf16(BM, BN / 2, 0u);  // split tiles (NK only)
   static constexpr uint32_t IDESC_PAIR = idesc_bf16(2 * BM, BN, 0u);   // PAIR (NK only)
@@ -122,7 +133,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
   float2* sXch = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);
   uint8_t* sGB = reinterpret_cast<uint8_t*>(sXch) + C::XCH_SMEM;  // [EPI_WARPS][gamma | beta]
-  uint8_t* sBar = sGB + C::GB_SMEM;
+  uint8_t* sGam = sGB + C::GB_SMEM;  // FUSE_RMS: gamma, bf16 [num_k_blocks * 64]
+  float* sRstd = reinterpret_cast<float*>(sGam + C::GAM_SMEM);  // FUSE_RMS: [2][BM]
+  uint8_t* sBar = reinterpret_cast<uint8_t*>(sRstd) + C::RSTD_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
   uint64_t* conv = empty + C::STAGES;
@@ -131,7 +144,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint64_t* drain = tempty + 2;
   uint64_t* sready = drain + 1;  // FUSE_LN: row partials of both CTAs are in sXch[acc]
   uint64_t* rbar = sready + 2;   // FUSE_LN: [EPI_WARPS] a warp's residual boxes have landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + (C::LN ? C::EPI_WARPS : 0));
+  uint64_t* rfull = rbar + (C::LN ? C::EPI_WARPS : 0);  // FUSE_RMS: sRstd[acc] is written
+  uint64_t* rempty = rfull + 2;                          // FUSE_RMS: sRstd[acc] was read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + (C::RMS ? 2 : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -142,7 +157,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 128);
+      mbar_init(&conv[s], C::CONV_COUNT > 0 ? C::CONV_COUNT : 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -153,6 +168,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     if (C::LN) {
       for (int a = 0; a < 2; ++a) mbar_init(&sready[a], 2 * C::EPI_WARPS * 32);
       for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&rbar[w], 1);
+    }
+    if (C::RMS) {
+      for (int a = 0; a < 2; ++a) {
+        mbar_init(&rfull[a], 128);
+        mbar_init(&rempty[a], C::EPI_WARPS * 32);
+      }
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -310,7 +331,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          uint64_t* ready = (WMODE == W_I8_NK) ? &conv[stage] : &full[stage];
+          uint64_t* ready = C::CONV_COUNT > 0 ? &conv[stage] : &full[stage];
           if (!mbar_wait(ready, phase, abort_flag, 3)) {
             ok = false;
             break;
@@ -413,6 +434,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         rph ^= 1;
         res_pending = false;
       }
+      float row_rstd = 1.f;  // FUSE_RMS: 1 / rms of this row
+      if constexpr (C::RMS) {
+        if (!mbar_wait(&rfull[acc], acc_phase, abort_flag, 12)) break;
+        row_rstd = sRstd[acc * BM + row];
+        mbar_arrive(&rempty[acc]);
+      }
       __syncwarp();
       tc_fence_after();
       const int m = mt * BM + row;
@@ -481,6 +508,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
                                                         ((q ^ ((lane >> 1) & 3)) << 4));
           }
           uint32_t packed[16];
+          if constexpr (C::RMS) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) cur[i] *= row_rstd;
+          }
           epilogue_math<EPI>(p, m, n0, cur,
                              ((kPrefetch || res_box) && n0 + 32 <= p.N) ? rcur : nullptr, packed);
           if (C::LN) tmem_st16w(tbase + (uint32_t)(c * 32), packed);  // Y, for the norm pass
@@ -635,7 +666,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     if (res_pending) mbar_wait(&rbar[e], rph, nullptr, 11);
     if (C::LN) grid_dep_launch();
     if (lane == 0) bulk_wait<0>();  // stores complete before the CTA exits
-  } else if (WMODE == W_I8_NK) {
+  } else if (WMODE == W_I8_NK && warp < C::NORM_WARP0) {
     // ── int8 -> bf16 converter (4 warps) ──
     const int t = threadIdx.x - 32 * C::CONV_WARP0;
     int stage = 0;
@@ -652,13 +683,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         for (int i = t; i < BN * 4; i += 128) {
           const int n = i >> 2;
           const int c = i & 3;  // 16 int8 along K: k = 16c .. 16c+15
-          const int4 raw = *reinterpret_cast<const int4*>(src + n * 64 + c * 16);
-          const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
-          float f[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) f[j] = (float)b[j];
-          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c)) = pack8(f);
-          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c + 1)) = pack8(f + 8);
+          const uint4 raw = *reinterpret_cast<const uint4*>(src + n * 64 + c * 16);
+          uint4 o0, o1;
+          i8x4_to_bf16x4(raw.x, o0.x, o0.y);
+          i8x4_to_bf16x4(raw.y, o0.z, o0.w);
+          i8x4_to_bf16x4(raw.z, o1.x, o1.y);
+          i8x4_to_bf16x4(raw.w, o1.z, o1.w);
+          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c)) = o0;
+          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c + 1)) = o1;
         }
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
@@ -667,6 +699,65 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           phase ^= 1;
         }
       }
+    }
+  } else if (C::RMS) {
+    // ── RMSNorm of A (4 warps): thread t owns row t of every A tile. It scales
+    // the row's 64 values of each stage by gamma in place (bf16, the layout
+    // the MMA reads), sums their squares, and at the end of the tile's K loop
+    // hands the row's 1 / sqrt(sum / K + eps) to the epilogue. ──
+    const int t = threadIdx.x - 32 * C::NORM_WARP0;
+    {
+      // gamma over K, zero past K (the TMA zero-fills A past K as well)
+      __nv_bfloat16* g = reinterpret_cast<__nv_bfloat16*>(sGam);
+      const int kpad = p.num_k_blocks * BK;
+      for (int k = t; k < kpad; k += 128)
+        g[k] = k < p.K ? p.rms_gamma[k] : __float2bfloat16_rn(0.f);
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four norm warps only
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = tile0; tile < num_tiles && ok; tile += tstep) {
+      float ss0 = 0.f, ss1 = 0.f;
+      for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, 13)) {
+          ok = false;
+          break;
+        }
+        uint8_t* rowp = sA + stage * C::A_BYTES + t * 128;
+        const uint4* gk = reinterpret_cast<const uint4*>(sGam + kb * (BK * 2));
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4* q = reinterpret_cast<uint4*>(rowp + ((c ^ (t & 7)) << 4));
+          const uint4 x = *q;
+          const uint4 gv = gk[c];  // (the same address for every lane: a broadcast)
+          const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+          uint32_t yw[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float a0 = bf16_lo(xw[j]), a1 = bf16_hi(xw[j]);
+            ss0 = fmaf(a0, a0, ss0);
+            ss1 = fmaf(a1, a1, ss1);
+            yw[j] = cvt_bf16x2(a0 * bf16_lo(gw[j]), a1 * bf16_hi(gw[j]));
+          }
+          *q = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[stage]);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (!mbar_wait(&rempty[acc], acc_phase ^ 1, abort_flag, 14)) break;
+      sRstd[acc * BM + t] = 1.0f / sqrtf((ss0 + ss1) / (float)p.K + p.norm_eps);
+      mbar_arrive(&rfull[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
     }
   }
 
@@ -721,7 +812,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return finish_launch(cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, ty2, tr, a));
+  return launch_cfg(cfg, kern, ta, tb, ty, ty2, tr, a);
 }
 
 // (dispatch value for a 2-SM pair launch, beside the gemm::Fuse modes)
@@ -733,12 +824,18 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
                  const GemmArgs& a, cudaStream_t st) {
   using gemm::FUSE_LN;
   using gemm::FUSE_NONE;
+  using gemm::FUSE_RMS;
   // every instantiation takes the second output map; only FUSE_LN writes it
   if (fuse == FUSE_PAIR) {
     if constexpr (BN == 256 && WMODE == W_BF16_NK) {
       if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
       if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
     }
+    return CK_ERR_UNSUPPORTED;
+  }
+  if (fuse == FUSE_RMS) {
+    if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_RMS>(ta, tb, ty0, ty2, tr, a, st);
+    if (epi == CK_EPI_BIAS) return launch_gemm<BN, WMODE, CK_EPI_BIAS, FUSE_RMS>(ta, tb, ty0, ty2, tr, a, st);
     return CK_ERR_UNSUPPORTED;
   }
   if (fuse == FUSE_LN) {
@@ -818,6 +915,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   if (w_dtype == CK_I8 && w_scale == nullptr) return CK_ERR_INVALID_ARG;
   a.scale_vec = (reinterpret_cast<uintptr_t>(w_scale) & 15u) == 0;
   a.norm_eps = 0.f;
+  a.rms_gamma = nullptr;
   a.ln_gamma = nullptr;
   a.ln_beta = nullptr;
   a.res_tma = 0;
@@ -837,6 +935,14 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     a.ln_beta = reinterpret_cast<const __nv_bfloat16*>(fz->ln_beta);
     a.norm_eps = fz->eps;
     fuse = gemm::FUSE_LN;
+  } else if (fz != nullptr && fz->rms_gamma != nullptr) {
+    // RMSNorm of A in the GEMM: gamma staged over all of K in shared memory
+    using CR = GemmCfg<256, W_BF16_NK, gemm::FUSE_RMS, CK_EPI_STORE>;
+    if (K > CR::RMS_KMAX || (epi != CK_EPI_STORE && epi != CK_EPI_BIAS))
+      return CK_ERR_UNSUPPORTED;
+    a.rms_gamma = reinterpret_cast<const __nv_bfloat16*>(fz->rms_gamma);
+    a.norm_eps = fz->eps;
+    fuse = gemm::FUSE_RMS;
   }
 
   // 2-SM pairs (256-row tiles, B split over the pair): bf16 (N, K) weights, a

@@ -546,7 +546,7 @@ int launch_head(const CUtensorMap& tx, const CUtensorMap& tb, const HeadArgs& a,
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return finish_launch(cudaLaunchKernelEx(&cfg, kern, tx, tb, a));
+  return launch_cfg(cfg, kern, tx, tb, a);
 }
 
 }  // namespace

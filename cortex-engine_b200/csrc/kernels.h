@@ -17,6 +17,23 @@ bool smem_attr_ready(const void* kernel, int bytes);  // per device, once
 bool pdl_enabled();       // CK_PDL=0 in the environment turns programmatic launch off
 int finish_launch(cudaError_t e);  // counts the launch; CK_OK or CK_ERR_CUDA
 
+// Launch trace (trace.cpp): while ck_trace_begin is active, every launch of
+// this library outside a stream capture is bracketed by two CUDA events on its
+// stream, so that the host can read each kernel's device time afterwards.
+extern int g_trace_on;
+void trace_before(cudaStream_t st);
+void trace_after(cudaStream_t st, const void* func);
+
+// Every kernel of the library goes through this launch: trace events when
+// tracing is on, then the launch itself and its status.
+template <typename... KArgs, typename... Args>
+int launch_cfg(const cudaLaunchConfig_t& cfg, void (*kernel)(KArgs...), Args&&... args) {
+  if (g_trace_on) trace_before(cfg.stream);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+  if (g_trace_on) trace_after(cfg.stream, reinterpret_cast<const void*>(kernel));
+  return finish_launch(e);
+}
+
 // Launch a kernel with programmatic stream serialisation: the grid may be
 // scheduled while the previous kernel in the stream is finishing, and waits
 // for it inside the kernel (grid_dep_wait in common.cuh). Captured into a CUDA
@@ -34,7 +51,7 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return finish_launch(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
+  return launch_cfg(cfg, kernel, static_cast<Args&&>(args)...);
 }
 
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
@@ -45,9 +62,10 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
 bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_layout, int64_t N,
                        int64_t ldw, const void* A, const void* W, int64_t ldy, const void* Y,
                        int epi, const void* aux, int64_t ld_aux);
-// Optional epilogue fusion of the tcgen05 GEMM (see gemm_common.cuh):
+// Optional fusions of the tcgen05 GEMM (see gemm_common.cuh):
 //   ln_out     residual epilogue also writes LayerNorm(Y) (gamma ln_gamma, beta
 //              ln_beta or none, eps) to ln_out (row stride ln_ld): bf16, N = 512
+//   rms_gamma  RMSNorm of the A rows (gamma rms_gamma, eps) applied inside the GEMM
 struct GemmFusion {
   float eps = 0.f;
   void* ln_out = nullptr;
@@ -58,6 +76,9 @@ struct GemmFusion {
   // (model weights inside the forward): its first tiles may load before the
   // GEMM's dependency wait
   bool w_static = false;
+  // RMSNorm of A fused into the GEMM (bf16 A, K <= 4096, store or bias
+  // epilogue): y = epi((x * gamma) W^T * (1 / sqrt(mean_k(x^2) + eps)))
+  const void* rms_gamma = nullptr;
 };
 // Tensor-core GEMM when supported, else the CUDA-core one (capi.cu).
 // w_static: the weight is not written by the kernel launched just before on
@@ -67,6 +88,20 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
                     int w_dtype, int w_layout, int64_t N, int64_t ldw, const float* w_scale,
                     int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
                     int64_t ldy, cudaStream_t st, bool w_static = false);
+// Norm then linear (capi.cu). RMSNorm over bf16 rows that the tcgen05 GEMM
+// takes (K <= 4096, store or bias epilogue) runs as one launch with the norm
+// inside the GEMM (norm_linear_fused); every other case writes the normalised
+// rows to the workspace (M * K elements of dtype) and runs the linear after
+// it, and returns CK_ERR_WORKSPACE without launching when that is too small.
+bool norm_linear_fused(int dtype, int64_t M, int64_t K, int64_t ldx, const void* x,
+                       const void* gamma, int norm_mode, const void* W, int w_dtype,
+                       int w_layout, int64_t N, int64_t ldw, int epi, const void* aux,
+                       int64_t ld_aux, const void* Y, int64_t ldy);
+int norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* gamma,
+                const void* beta, float eps, int norm_mode, const void* W, int w_dtype,
+                int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi,
+                const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y, int64_t ldy,
+                void* workspace, size_t workspace_bytes, cudaStream_t st);
 int gemm_tc_block_n(int64_t N);
 int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int w_dtype,
             int w_layout, int64_t N, int64_t ldw, const float* w_scale, int epi, const void* aux,

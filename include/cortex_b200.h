@@ -61,6 +61,23 @@ int ck_num_sms(void);
 /* Kernel launches issued by this library since it was loaded (all threads). */
 long long ck_launch_count(void);
 
+/* Launch trace, for measurement: between ck_trace_begin and ck_trace_end every
+ * kernel the library launches outside a stream capture is bracketed by two
+ * CUDA events on its own stream (up to `capacity` launches; later ones are
+ * not timed). ck_trace_end synchronises on the events and writes one record
+ * per traced launch, in launch order, to out[0 .. min(n, capacity)), with *n
+ * the number traced. The events sit between launches, so a traced kernel does
+ * not overlap its predecessor: each figure is that kernel's own device time.
+ * No reference counterpart (the reference times kernels with torch profilers,
+ * benchmarks/profiling/). */
+typedef struct ck_trace_record {
+  char name[96]; /* kernel name with template arguments, no namespaces */
+  void* stream;  /* cudaStream_t the kernel ran on */
+  float ms;      /* device time between the two events (-1 on error) */
+} ck_trace_record;
+int ck_trace_begin(int32_t capacity);
+int ck_trace_end(ck_trace_record* out, int32_t capacity, int32_t* n);
+
 /* ── 1. event packing ───────────────────────────────────────────────────────
  * Replaces _pack_events' index work (cortex/models/cortex.py:125-165):
  * bincount (:141), E_max (:142), stable argsort (:149), exclusive cumsum (:155-160),
@@ -117,7 +134,16 @@ int ck_linear(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const
 
 /* Norm then linear: replaces rms_norm_linear (cortex/kernels/fused_rmsnorm.py:239-301)
  * with norm_mode = CK_NORM_RMS, and LayerNorm->Linear pairs of the model with
- * CK_NORM_LAYER. workspace must hold M*K elements of dtype. */
+ * CK_NORM_LAYER. RMSNorm of bf16 rows runs as ONE launch when the tensor-core
+ * GEMM takes the shapes (16-byte aligned rows, K <= 4096) and the epilogue is
+ * CK_EPI_STORE or CK_EPI_BIAS: the GEMM scales every A tile by gamma in shared
+ * memory, sums x^2 per row on the way, and multiplies each output row by
+ * 1 / sqrt(sum / K + eps) in its epilogue, so x is read once and no normalised
+ * copy exists (the reference's kernel reads x twice, :130-233). That path
+ * needs no workspace (NULL is fine). Every other call normalises into the
+ * workspace (M*K elements of dtype; ck_norm_linear_workspace_bytes) and runs
+ * the linear after it; it returns CK_ERR_WORKSPACE, launching nothing, when the
+ * workspace is missing or too small. gamma is required. */
 size_t ck_norm_linear_workspace_bytes(int dtype, int64_t M, int64_t K);
 int ck_norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* gamma,
                    const void* beta, float eps, int norm_mode, const void* W, int w_dtype,
@@ -128,15 +154,17 @@ int ck_norm_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, 
 /* ck_norm_linear without a caller-provided workspace, for callers that cannot
  * allocate device memory (a host runtime binding this ABI without a CUDA
  * allocator of its own, or a serving loop that must not allocate once running).
- * No counterpart in the reference: it is an addition of this library. The
- * normalised activations go to a fixed 8 MiB array in device memory that the
- * library defines (held by every GPU that loads it until the process exits):
- * M*K elements of dtype must fit in CK_NORM_LINEAR_STATIC_SCRATCH_BYTES, or the
- * call returns CK_ERR_INVALID_ARG without launching anything. All calls on a
- * device share that array, so calls that overlap on the GPU race and must be
- * serialised by the caller. The first call on each device looks up the array's
- * address; make it before any stream capture. Same arguments and results as
- * ck_norm_linear otherwise. */
+ * No counterpart in the reference: it is an addition of this library. Calls
+ * that ck_norm_linear runs as one launch need no scratch; on the two-launch
+ * path the normalised activations go to a fixed 8 MiB array in device memory
+ * that the library defines (held by every GPU that loads it until the process
+ * exits): M*K elements of dtype must fit in CK_NORM_LINEAR_STATIC_SCRATCH_BYTES,
+ * or the call returns CK_ERR_INVALID_ARG without launching anything. All calls
+ * on a device share that array, so calls that overlap on the GPU race and must
+ * be serialised by the caller. Each call looks the array's address up on the
+ * current device; the first call on a device also loads the library's device
+ * code there, so make it before any stream capture. Same arguments and results
+ * as ck_norm_linear otherwise (CK_NORM_NONE runs the plain linear). */
 #define CK_NORM_LINEAR_STATIC_SCRATCH_BYTES (8u << 20)
 int ck_norm_linear_static(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                           const void* gamma, const void* beta, float eps, int norm_mode,

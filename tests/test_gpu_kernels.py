@@ -15,6 +15,7 @@ import numpy as np
 import pytest
 import torch
 
+from cortex import _lib as L
 from oracle import cortex_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -363,11 +364,85 @@ def test_rms_norm_linear(M, K, N, dtype):
         ref = O.rms_norm_linear(x, gamma, w, None)
         torch.testing.assert_close(out.cpu(), ref, rtol=1e-4, atol=1e-4)
     else:
-        # reference rounding points, fp32 accumulation of the bf16 product
-        xf = x.float()
-        xn = ((xf / torch.sqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)) * gamma.float())
-        ref = (xn.to(dtype).float() @ w.float()).to(dtype)
-        torch.testing.assert_close(out.cpu(), ref, rtol=1e-2, atol=1e-1)
+        # The reference test's bf16 tolerance (tests/unit/test_kernel_fused_rmsnorm.py:
+        # rtol 1e-2, atol 1e-1) against the exact result of the same bf16 inputs
+        # (fp64): the one-launch kernel applies 1 / rms to the fp32 product, so it
+        # carries no rounding of x / rms to bf16. The reference's eager bf16 path
+        # does (rms_norm_linear_reference), and at these sizes it is itself outside
+        # that tolerance of the exact result for a few thousand elements, so against
+        # it the check is norm-wise.
+        xd = x.double()
+        exact = (xd / torch.sqrt(xd.pow(2).mean(-1, keepdim=True) + 1e-6)
+                 * gamma.double()) @ w.double()
+        torch.testing.assert_close(out.cpu().double(), exact, rtol=1e-2, atol=1e-1)
+        ref = O.rms_norm_linear(x, gamma, w, None).double()
+        assert ((out.cpu().double() - ref).norm() / ref.norm()).item() <= 1e-2
+
+
+def _norm_linear_call(x, g, w, sc, bias, ws=None):
+    """ck_norm_linear (RMS) through the C ABI; w (K, N) bf16 or (N, K) int8."""
+    M, K = x.shape
+    if sc is not None:
+        N = w.shape[0]
+        wargs = (w.data_ptr(), L.CK_I8, L.CK_W_NK, N, K, sc.data_ptr())
+    else:
+        N = w.shape[1]
+        wargs = (w.data_ptr(), L.CK_BF16, L.CK_W_KN, N, N, None)
+    y = torch.empty(M, N, dtype=x.dtype, device=DEV)
+    epi = L.CK_EPI_BIAS if bias is not None else L.CK_EPI_STORE
+    rc = L.load().ck_norm_linear(x.data_ptr(), L.CK_BF16, M, K, K, g.data_ptr(), None, 1e-6,
+                                 L.CK_NORM_RMS, *wargs, epi, L.ptr(bias), 0, 0, y.data_ptr(), N,
+                                 L.ptr(ws), 0 if ws is None else ws.numel(),
+                                 L.stream_of(x.device))
+    return rc, y
+
+
+@pytest.mark.parametrize("M,K,N", [(8192, 512, 1536), (8192, 512, 2048), (1000, 768, 256),
+                                   (130, 4096, 384), (64, 64, 128)])
+@pytest.mark.parametrize("wkind", ["bf16", "int8"])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_norm_linear_fused_single_launch(M, K, N, wkind, with_bias):
+    """RMSNorm + linear of bf16 rows is ONE tcgen05 launch with no workspace:
+    the norm warps scale the TMA-loaded tiles by gamma and sum x^2 per row,
+    the epilogue applies 1 / rms. Checked against the oracle's restatement of
+    rms_norm_linear_reference (normalised rows rounded to bf16 before the
+    product; int8 weights dequantised as QuantizedLinear does)."""
+    torch.manual_seed(K + N)
+    x = torch.randn(M, K, dtype=torch.bfloat16) * 3 + 0.5
+    g = (torch.rand(K) + 0.5).to(torch.bfloat16)
+    bias = torch.randn(N, dtype=torch.bfloat16) if with_bias else None
+    if wkind == "int8":
+        w8 = torch.randint(-127, 128, (N, K), dtype=torch.int8)
+        sc = (torch.rand(N) + 0.5) / 127.0
+        w_ref = (w8.float() * sc[:, None]).to(torch.bfloat16).t().contiguous()  # (K, N)
+        wd, scd = w8.to(DEV), sc.to(DEV)
+    else:
+        w_ref = torch.randn(K, N, dtype=torch.bfloat16) / math.sqrt(K)
+        wd, scd = w_ref.to(DEV), None
+    xd, gd = x.to(DEV), g.to(DEV)
+    bd = bias.to(DEV) if bias is not None else None
+    n0 = L.load().ck_launch_count()
+    rc, y = _norm_linear_call(xd, gd, wd, scd, bd)  # no workspace
+    assert rc == L.CK_OK, L.status_string(rc)
+    assert L.load().ck_launch_count() - n0 == 1
+    _status_ok()
+    ref = O.rms_norm_linear(x, g, w_ref, bias).float()
+    out = y.float().cpu()
+    assert torch.isfinite(out).all()
+    rel = ((out - ref).norm() / ref.norm()).item()
+    assert rel <= 1e-2, rel
+    torch.testing.assert_close(out, ref, rtol=2e-2, atol=5e-2 * ref.abs().max().item() / 8)
+
+
+def test_norm_linear_fallback_asks_for_workspace():
+    """Calls the one-launch path does not take (K not 16-byte aligned here)
+    return CK_ERR_WORKSPACE without launching when no workspace is given."""
+    x = torch.randn(33, 70, dtype=torch.bfloat16, device=DEV)
+    g = torch.ones(70, dtype=torch.bfloat16, device=DEV)
+    w = torch.randn(70, 97, dtype=torch.bfloat16, device=DEV)
+    n0 = L.load().ck_launch_count()
+    rc, _ = _norm_linear_call(x, g, w, None, None)
+    assert rc == L.CK_ERR_WORKSPACE and L.load().ck_launch_count() == n0
 
 
 def test_rms_norm_linear_bias_and_3d(golden_kernels):
@@ -385,6 +460,13 @@ def test_rms_norm_linear_bias_and_3d(golden_kernels):
     assert out.shape == (2, 256, 1536)
     ref = O.rms_norm_linear(x.reshape(512, 512), torch.ones(512), w, None).reshape(2, 256, 1536)
     torch.testing.assert_close(out.cpu(), ref, rtol=1e-4, atol=1e-4)
+    # bf16, 3-D, bias and gamma: the one-launch path behind the reference API
+    xb, wb = x.to(torch.bfloat16), (w / 16).to(torch.bfloat16)
+    gb = (torch.rand(512) + 0.5).to(torch.bfloat16)
+    bb = torch.randn(1536, dtype=torch.bfloat16)
+    out = rms_norm_linear(xb.to(DEV), gb.to(DEV), wb.to(DEV), bb.to(DEV)).float().cpu()
+    ref = O.rms_norm_linear(xb.reshape(512, 512), gb, wb, bb).reshape(2, 256, 1536).float()
+    assert ((out - ref).norm() / ref.norm()).item() <= 1e-2
 
 
 # ── attention ────────────────────────────────────────────────────────────────

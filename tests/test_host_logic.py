@@ -50,7 +50,7 @@ def test_ctypes_structs_match_header_layout(tmp_path):
     if shutil.which("gcc") is None:
         pytest.skip("gcc not available")
     structs = {"ck_attention_args": _lib.AttentionArgs, "ck_linear_weight": _lib.LinearWeight,
-               "ck_block_weights": _lib.BlockWeights,
+               "ck_block_weights": _lib.BlockWeights, "ck_trace_record": _lib.TraceRecord,
                "ck_model": _lib.Model}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "cortex_b200.h"',
              'int main(void) {']
@@ -189,3 +189,19 @@ def test_int8_workload_converts_exactly_the_self_attention_linears():
     q = {n for n, m in model.named_modules() if isinstance(m, QuantizedLinear)}
     assert q == set(int8_layer_names(wl.config)) and len(q) == 28
     assert model.tokenizer.neuron_emb.weight.dtype == torch.bfloat16
+
+
+def test_int8_to_bf16_bit_trick_is_exact_for_every_byte():
+    """The GEMM widens int8 weight tiles to bf16 with byte permutes and one fp32
+    subtraction (i8x4_to_bf16x4 in csrc/common.cuh): byte b ^ 0x80 in the low
+    byte of the fp32 word 0x4B000000 is 2^23 + 128 + v; minus (2^23 + 128) it is
+    v, and the upper 16 bits of that fp32 are bf16(v). Restated in numpy for all
+    256 byte values against torch's own int8 -> bf16 conversion."""
+    v = np.arange(-128, 128, dtype=np.int8)
+    u = (v.view(np.uint8) ^ 0x80).astype(np.uint32)
+    word = (0x4B000000 | u).astype(np.uint32)
+    f = word.view(np.float32) - np.float32(8388736.0)
+    assert np.array_equal(f, v.astype(np.float32))
+    bf = (f.view(np.uint32) >> 16).astype(np.uint16)
+    ref = torch.from_numpy(v.copy()).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(bf, ref)
