@@ -37,7 +37,8 @@ bool norm_linear_fused(int dtype, int64_t M, int64_t K, int64_t ldx, const void*
                        const void* gamma, int norm_mode, const void* W, int w_dtype,
                        int w_layout, int64_t N, int64_t ldw, int epi, const void* aux,
                        int64_t ld_aux, const void* Y, int64_t ldy) {
-  return norm_mode == CK_NORM_RMS && dtype == CK_BF16 && gamma != nullptr && K <= 4096 &&
+  return norm_mode == CK_NORM_RMS && dtype == CK_BF16 && gamma != nullptr && K % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(gamma) & 15u) == 0 &&
          (epi == CK_EPI_STORE || epi == CK_EPI_BIAS) && (w_dtype == CK_BF16 || w_dtype == CK_I8) &&
          gemm_tc_supported(M, K, ldx, w_dtype, w_layout, N, ldw, x, W, ldy, Y, epi, aux, ld_aux);
 }

@@ -173,26 +173,26 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 
 // Four int8 values (one 32-bit word, little-endian) to four bf16 values, exact,
-// on the integer and FMA pipes rather than the conversion unit (I2F and F2F
-// issue at a fraction of the FMA rate; with one I2F per element and one F2F per
-// pair they made the int8 weight tiles the slowest stage of the GEMM pipeline). Each byte, flipped to the unsigned v + 128, is
-// placed in the low byte of the fp32 word 0x4B000000 (2^23, whose last place is
-// 1), so the word holds 2^23 + 128 + v exactly; one paired subtraction leaves v.
-// An fp32 integer of magnitude <= 128 has at most 8 significant bits, so its
-// upper 16 bits are its bf16 value, and one byte permute packs two of them.
+// with integer logic and one bf16x2 subtraction per pair, never the conversion
+// unit (I2F and F2F issue at a fraction of the FMA rate; with one I2F per
+// element and one F2F per pair they made the int8 weight tiles the slowest
+// stage of the GEMM pipeline). For a byte v (two's complement), the bf16 with
+// exponent 2^7 and mantissa v & 0x7F is 128 + (v & 127), which is 128 + v for
+// v >= 0 and 256 + v for v < 0; subtracting the bf16 whose mantissa is the
+// sign bit, 128 or 256, leaves v, exactly (every integer of magnitude <= 256
+// is a bf16). One byte permute first orders the word (b0, b2, b1, b3), so the
+// even / odd 16-bit lanes hold (b0, b1) and (b2, b3), the output pairs.
+__device__ __forceinline__ uint32_t sub_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const uint32_t magic = 0x4B000000u;
-  const unsigned long long bias = f2pk(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-  float a0, a1, a2, a3;
-  f2up(fadd2(f2pk(__uint_as_float(prmt(u, magic, 0x7540u)), __uint_as_float(prmt(u, magic, 0x7541u))),
-             bias),
-       a0, a1);
-  f2up(fadd2(f2pk(__uint_as_float(prmt(u, magic, 0x7542u)), __uint_as_float(prmt(u, magic, 0x7543u))),
-             bias),
-       a2, a3);
-  lo = prmt(__float_as_uint(a0), __float_as_uint(a1), 0x7632u);
-  hi = prmt(__float_as_uint(a2), __float_as_uint(a3), 0x7632u);
+  const uint32_t r = prmt(w, 0u, 0x3120u);  // bytes (b0, b2, b1, b3)
+  const uint32_t r8 = r >> 8;               // (b2, ., b3, .) in the low bytes of the halves
+  lo = sub_bf16x2((r & 0x007F007Fu) | 0x43004300u, (r & 0x00800080u) | 0x43004300u);
+  hi = sub_bf16x2((r8 & 0x007F007Fu) | 0x43004300u, (r8 & 0x00800080u) | 0x43004300u);
 }
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -276,6 +276,24 @@ __device__ __forceinline__ void gelu32(float* v) {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte shared-memory load / store by shared-window address (smem_u32).
+// The kernels align their dynamic shared memory by integer arithmetic, after
+// which the compiler no longer knows a pointer is shared; these keep the
+// accesses on the shared-memory path instead of generic loads and stores.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 // ── mbarrier ─────────────────────────────────────────────────────────────────
@@ -362,6 +380,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// try_wait with a suspend-time hint (ns): while the phase is incomplete the
+// thread is parked by the hardware, issuing nothing, until the phase completes
+// or the hint expires.
+__device__ __forceinline__ bool mbar_try_wait_ns(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for roles that wait long and whose wake-up latency is not on
+// the critical path (the epilogue waiting out a tile's main loop, the TMA
+// producer waiting for a free stage, the operand transform warps waiting for
+// their next stage): the thread is parked between checks, so that the warps
+// sharing its scheduler -- the ones doing the work -- get its issue slots.
+// Same timeout and abort behaviour as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_park(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait_ns(bar, parity, 20000u)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      set_status(CK_ERR_TIMEOUT, site, (int)parity);
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 // ── thread-block clusters (distributed shared memory) ─────────────────────────
 
 __device__ __forceinline__ uint32_t cl_rank() {
@@ -379,6 +433,12 @@ __device__ __forceinline__ uint32_t cl_map(const void* local, uint32_t rank) {
 
 __device__ __forceinline__ void cl_store_f2(uint32_t remote, float2 v) {
   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(remote), "f"(v.x), "f"(v.y)
+               : "memory");
+}
+
+__device__ __forceinline__ void cl_store_v4(uint32_t remote, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
 

@@ -54,6 +54,10 @@ using gemm::epilogue_math;
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int STG_BOX = 32 * 32 * 2;  // one 32-row x 32-col bf16 store box (64B rows)
+// FUSE_LN: each warp's columns in 32-row x 64-col boxes (128B rows, 128B
+// swizzle), two 32-column chunks per box, so that the residual loads and the
+// two output stores take half as many TMA commands
+constexpr int LN_BOX = 32 * 64 * 2;
 
 enum WMode { W_BF16_NK = 0, W_BF16_KN = 1, W_I8_NK = 2 };
 
@@ -70,7 +74,7 @@ struct GemmCfg {
   // lies on the critical path (one tile per CTA); two per quarter otherwise
   // (and always in int8 mode, whose converter warps need the registers)
   static constexpr bool LN = FUSE == 3;   // gemm::FUSE_LN
-  static constexpr bool RMS = FUSE == 4;  // gemm::FUSE_RMS
+  static constexpr bool RMS = FUSE == 4;  // gemm::FUSE_RMS: a norm warpgroup scales the A tiles
   static constexpr int EPI_WARPS =
       (WMODE != W_I8_NK && (EPI == CK_EPI_GELU || LN)) ? 16 : 8;
   static constexpr int EPI_GROUPS = EPI_WARPS / 4;  // column slices of a tile
@@ -92,26 +96,28 @@ struct GemmCfg {
   // (two warps per lane quarter only: with four, the pipeline ring needs the room
   // and the norm pass reads them through the read-only cache)
   static constexpr int GB_SMEM = (LN && EPI_WARPS == 8) ? EPI_WARPS * 2 * EPI_COLS * 2 : 0;
-  // FUSE_RMS: gamma over all of K (bf16, zero past K), staged once per CTA,
-  // and the per-row 1 / rms of each TMEM accumulator buffer
-  static constexpr int RMS_KMAX = 4096;
-  static constexpr int GAM_SMEM = RMS ? RMS_KMAX * 2 : 0;
-  static constexpr int RSTD_SMEM = RMS ? 2 * BM * 4 : 0;
-  static constexpr int BUDGET = 232448 - 1024 - BAR_BYTES - EPI_SMEM - XCH_SMEM - GB_SMEM -
-                                GAM_SMEM - RSTD_SMEM;
+  // FUSE_RMS: the per-row 1 / rms of each TMEM accumulator buffer (gamma
+  // comes through the read-only cache, so that the ring keeps its stages)
+  // FUSE_RMS norm warps: eight (two per scheduler, each thread half a row of a
+  // stage) with bf16 weights, four (a whole row each) beside the int8
+  // converter warps, whose registers they would otherwise take
+  static constexpr int RMS_WARPS = !RMS ? 0 : (WMODE == W_I8_NK ? 4 : 8);
+  static constexpr int RMS_SPLIT = RMS ? RMS_WARPS / 4 : 1;  // threads per row
+  static constexpr int RSTD_SMEM = RMS ? 2 * RMS_SPLIT * BM * 4 : 0;
+  static constexpr int BUDGET =
+      232448 - 1024 - BAR_BYTES - EPI_SMEM - XCH_SMEM - GB_SMEM - RSTD_SMEM;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   // bytes completing one stage's barrier (PAIR: both CTAs' loads, on the even CTA's)
   static constexpr int TX_BYTES = (PAIR ? 2 : 1) * (A_BYTES + (WMODE == W_I8_NK ? B8_BYTES : B_BYTES));
   static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
   static constexpr int NORM_WARP0 = CONV_WARP0 + (WMODE == W_I8_NK ? 4 : 0);
-  static constexpr int NUM_THREADS = 32 * (NORM_WARP0 + (RMS ? 4 : 0));
+  static constexpr int NUM_THREADS = 32 * (NORM_WARP0 + RMS_WARPS);
   // arrivals that make a stage's operands ready for the MMA after the TMA:
-  // the int8 converter and / or the RMS norm warpgroup, 128 threads each
-  static constexpr int CONV_COUNT = 128 * ((WMODE == W_I8_NK ? 1 : 0) + (RMS ? 1 : 0));
+  // the int8 converter and / or the norm warpgroup, 128 threads each
+  static constexpr int CONV_COUNT = 128 * (WMODE == W_I8_NK ? 1 : 0) + 32 * RMS_WARPS;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + EPI_SMEM + XCH_SMEM + GB_SMEM + GAM_SMEM + RSTD_SMEM +
-      BAR_BYTES;
+      1024 + STAGES * STAGE_BYTES + EPI_SMEM + XCH_SMEM + GB_SMEM + RSTD_SMEM + BAR_BYTES;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, WMODE == W_BF16_KN ? 1u : 0u);
   static constexpr uint32_t IDESC_HALF = idesc_bf16(BM, BN / 2, 0u);  // split tiles (NK only)
   static constexpr uint32_t IDESC_PAIR = idesc_bf16(2 * BM, BN, 0u);   // PAIR (NK only)
@@ -133,8 +139,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint8_t* sStg = sB8 + C::STAGES * C::B8_BYTES;  // 1 KB aligned (all sizes above are)
   float2* sXch = reinterpret_cast<float2*>(sStg + C::EPI_SMEM);
   uint8_t* sGB = reinterpret_cast<uint8_t*>(sXch) + C::XCH_SMEM;  // [EPI_WARPS][gamma | beta]
-  uint8_t* sGam = sGB + C::GB_SMEM;  // FUSE_RMS: gamma, bf16 [num_k_blocks * 64]
-  float* sRstd = reinterpret_cast<float*>(sGam + C::GAM_SMEM);  // FUSE_RMS: [2][BM]
+  // FUSE_RMS: per accumulator buffer, each row's sum of squares in RMS_SPLIT parts
+  float* sRstd = reinterpret_cast<float*>(sGB + C::GB_SMEM);  // [2][RMS_SPLIT][BM]
   uint8_t* sBar = reinterpret_cast<uint8_t*>(sRstd) + C::RSTD_SMEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(sBar);
   uint64_t* empty = full + C::STAGES;
@@ -142,7 +148,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
   uint64_t* tfull = conv + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* sready = drain + 1;  // FUSE_LN: row partials of both CTAs are in sXch[acc]
+  uint64_t* sready = drain + 1;  // FUSE_LN: row partials of both CTAs' warps are in sXch[acc]
   uint64_t* rbar = sready + 2;   // FUSE_LN: [EPI_WARPS] a warp's residual boxes have landed
   uint64_t* rfull = rbar + (C::LN ? C::EPI_WARPS : 0);  // FUSE_RMS: sRstd[acc] is written
   uint64_t* rempty = rfull + 2;                          // FUSE_RMS: sRstd[acc] was read
@@ -166,12 +172,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     }
     mbar_init(drain, 1);
     if (C::LN) {
-      for (int a = 0; a < 2; ++a) mbar_init(&sready[a], 2 * C::EPI_WARPS * 32);
+      for (int a = 0; a < 2; ++a) mbar_init(&sready[a], 2 * C::EPI_WARPS);  // a warp arrives once
       for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&rbar[w], 1);
     }
     if (C::RMS) {
       for (int a = 0; a < 2; ++a) {
-        mbar_init(&rfull[a], 128);
+        mbar_init(&rfull[a], 32 * C::RMS_WARPS);
         mbar_init(&rempty[a], C::EPI_WARPS * 32);
       }
     }
@@ -267,7 +273,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         int mt, nt, part;
         tile_mn(tile, mt, nt, part);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, 1)) break;
+          if (!mbar_wait_park(&empty[stage], phase ^ 1, abort_flag, 1)) break;
           if (PAIR) {
             // both CTAs' bytes complete on the even CTA's barrier, which alone
             // announces them
@@ -384,6 +390,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     constexpr int NCH = COLS / 32;  // 32-column chunks per warp per tile
     constexpr int NBOX = C::STG_WARP / STG_BOX;
     uint8_t* stg = sStg + e * C::STG_WARP;
+    // FUSE_LN: byte offset of 16-byte piece q of chunk c of this lane's row
+    auto ln_off = [&](int c, int q) -> uint32_t {
+      return (uint32_t)((c >> 1) * LN_BOX + lane * 128 + ((((c & 1) * 4 + q) ^ (lane & 7)) << 4));
+    };
     int acc = 0;
     uint32_t acc_phase = 0;
     // FUSE_LN: this warp's gamma | beta columns into shared memory (a CTA
@@ -403,8 +413,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         const int row0 = p.aux_row_mod > 0 ? (int)((int64_t)m0 % p.aux_row_mod) : m0;
         mbar_arrive_expect_tx(&rbar[e], C::STG_WARP);
 #pragma unroll
-        for (int c = 0; c < NCH; ++c)
-          tma_load_2d(stg + c * STG_BOX, &tmR, &rbar[e], nt * BN + half * COLS + c * 32, row0);
+        for (int c = 0; c < NCH; c += 2)
+          tma_load_2d(stg + (c >> 1) * LN_BOX, &tmR, &rbar[e], nt * BN + half * COLS + c * 32, row0);
       }
       res_pending = true;
     };
@@ -421,6 +431,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
               src != nullptr ? __ldg(reinterpret_cast<const uint4*>(src + n0) + k)
                              : make_uint4(0u, 0u, 0u, 0u);
           __syncwarp();
+        } else {
+          // gamma / beta go through the read-only cache in the second pass:
+          // bring this warp's 64 columns of each into L1 now, so that the
+          // second pass does not wait on L2 right after the row exchange
+          int mt, nt, part;
+          tile_mn(tile0, mt, nt, part);
+          const int n0 = nt * BN + half * COLS;
+          const __nv_bfloat16* src = lane == 0 ? p.ln_gamma : (lane == 1 ? p.ln_beta : nullptr);
+          if (src != nullptr)
+            for (int b = 0; b < COLS * 2; b += 128)
+              asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const uint8_t*>(src + n0) + b));
         }
         if (res_box) prefetch_res(tile0);
       }
@@ -428,16 +449,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     for (int tile = tile0; tile < num_tiles; tile += tstep) {
       int mt, nt, part;
       tile_mn(tile, mt, nt, part);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, 4)) break;
+      if (!mbar_wait_park(&tfull[acc], acc_phase, abort_flag, 4)) break;
       if (res_box) {
-        if (!mbar_wait(&rbar[e], rph, abort_flag, 10)) break;
+        if (!mbar_wait_park(&rbar[e], rph, abort_flag, 10)) break;
         rph ^= 1;
         res_pending = false;
       }
       float row_rstd = 1.f;  // FUSE_RMS: 1 / rms of this row
       if constexpr (C::RMS) {
-        if (!mbar_wait(&rfull[acc], acc_phase, abort_flag, 12)) break;
-        row_rstd = sRstd[acc * BM + row];
+        if (!mbar_wait_park(&rfull[acc], acc_phase, abort_flag, 12)) break;
+        float ss = 0.f;
+#pragma unroll
+        for (int h = 0; h < C::RMS_SPLIT; ++h) ss += sRstd[(acc * C::RMS_SPLIT + h) * BM + row];
+        row_rstd = 1.0f / sqrtf(ss / (float)p.K + p.norm_eps);
         mbar_arrive(&rempty[acc]);
       }
       __syncwarp();
@@ -504,8 +528,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           if (res_box) {  // the residual chunk from its box (this lane's row)
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              rcur[q] = *reinterpret_cast<const uint4*>(stg + c * STG_BOX + lane * 64 +
-                                                        ((q ^ ((lane >> 1) & 3)) << 4));
+              rcur[q] = lds128(smem_u32(stg + ln_off(c, q)));
           }
           uint32_t packed[16];
           if constexpr (C::RMS) {
@@ -553,8 +576,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           if (!C::LN) __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
-                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            sts128(smem_u32(C::LN ? stg + ln_off(c, q)
+                                  : box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)),
+                   make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]));
           if (!C::LN) {
             fence_proxy_async_smem();
             __syncwarp();
@@ -567,30 +591,48 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         if (kAhead && c + 1 < nch) tc_wait_ld();
       }
       if constexpr (C::LN) {
-        // the first pass's boxes (Y) go out together
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && m0 < p.M) {
-#pragma unroll
-          for (int c = 0; c < NCH; ++c) tma_store_2d(&tmY, stg + c * STG_BOX, nbase + c * 32, m0);
-          bulk_commit();
-        }
         // Row statistics: this warp's (mean, M2) over its COLS columns goes to
-        // its slot in both CTAs' shared memory (local store, DSMEM store), with
-        // one arrival on each CTA's barrier; the NP slots of a row then hold
-        // both CTAs' column slices.
+        // its slot in both CTAs' shared memory, with one arrival per warp on
+        // each CTA's barrier; the NP slots of a row then hold both CTAs' column
+        // slices. The lanes store their rows' partials locally (32 contiguous
+        // rows per warp); lane 0 copies the warp's 256 bytes to the partner
+        // (DSMEM) and arrives on both barriers, whose release at cluster scope
+        // covers its copies and, through the warp barrier, the lanes' stores.
+        // Lane 0 alone polls the barrier (acquire at cluster scope) and the
+        // warp barrier passes the partials on to the other lanes.
         constexpr int NP = 2 * C::EPI_GROUPS;
         const float mu = st_s1 / (float)COLS;
         const float2 part = make_float2(st_shift + mu, fmaxf(st_s2 - st_s1 * mu, 0.f));
         const uint32_t self = cl_rank();
         const uint32_t peer = self ^ 1u;
         float2* xb = sXch + acc * (NP * BM);
-        float2* mine = xb + ((int)self * C::EPI_GROUPS + half) * BM + row;
-        *mine = part;
-        cl_store_f2(cl_map(mine, peer), part);
-        mbar_arrive(&sready[acc]);
-        cl_mbar_arrive(cl_map(&sready[acc], peer));
-        if (!mbar_wait_cl(&sready[acc], acc_phase, abort_flag, 6)) break;
+        float2* mine = xb + ((int)self * C::EPI_GROUPS + half) * BM + quarter * 32;  // 32 rows
+        mine[lane] = part;
+        __syncwarp();
+        int xok = 1;
+        if (lane == 0) {
+          const uint32_t src = smem_u32(mine);
+          const uint32_t dst = cl_map(mine, peer);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) cl_store_v4(dst + 16 * i, lds128(src + 16 * i));
+          mbar_arrive(&sready[acc]);
+          cl_mbar_arrive(cl_map(&sready[acc], peer));
+        }
+        // the first pass's boxes (Y) go out while the partials cross over
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (m0 < p.M) {
+#pragma unroll
+            for (int c = 0; c < NCH; c += 2)
+              tma_store_2d(&tmY, stg + (c >> 1) * LN_BOX, nbase + c * 32, m0);
+            bulk_commit();
+          }
+          xok = mbar_wait_cl(&sready[acc], acc_phase, abort_flag, 6) ? 1 : 0;
+        }
+        xok = __shfl_sync(0xffffffffu, xok, 0);
+        __syncwarp();
+        if (!xok) break;
         float2 q[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) q[k] = xb[k * BM + row];
@@ -624,8 +666,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           for (int q4 = 0; q4 < 4; ++q4) {
             uint4 g, b;
             if constexpr (C::GB_SMEM > 0) {
-              g = *reinterpret_cast<const uint4*>(wgb + (c * 32 + q4 * 8) * 2);
-              b = *reinterpret_cast<const uint4*>(wgb + (COLS + c * 32 + q4 * 8) * 2);
+              g = lds128(smem_u32(wgb + (c * 32 + q4 * 8) * 2));
+              b = lds128(smem_u32(wgb + (COLS + c * 32 + q4 * 8) * 2));
             } else {
               g = __ldg(reinterpret_cast<const uint4*>(p.ln_gamma + n0) + q4);
               b = p.ln_beta != nullptr ? __ldg(reinterpret_cast<const uint4*>(p.ln_beta + n0) + q4)
@@ -643,18 +685,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
               normed[i] = cvt_bf16x2(y0, y1);
             }
           }
-          // box c was read by the first pass's store (waited for above)
-          uint8_t* box = stg + c * STG_BOX;
+          // the boxes were read by the first pass's stores (waited for above)
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
-                make_uint4(normed[4 * q], normed[4 * q + 1], normed[4 * q + 2], normed[4 * q + 3]);
+            sts128(smem_u32(stg + ln_off(c, q)),
+                   make_uint4(normed[4 * q], normed[4 * q + 1], normed[4 * q + 2], normed[4 * q + 3]));
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && m0 < p.M) {
 #pragma unroll
-          for (int c = 0; c < NCH; ++c) tma_store_2d(&tmY2, stg + c * STG_BOX, nbase + c * 32, m0);
+          for (int c = 0; c < NCH; c += 2) tma_store_2d(&tmY2, stg + (c >> 1) * LN_BOX, nbase + c * 32, m0);
           bulk_commit();
         }
       }
@@ -674,23 +715,30 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
     bool ok = true;
     for (int tile = tile0; tile < num_tiles && ok; tile += tstep) {
       for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort_flag, 5)) {
+        if (!mbar_wait_park(&full[stage], phase, abort_flag, 5)) {
           ok = false;
           break;
         }
         const uint8_t* src = sB8 + stage * C::B8_BYTES;
         uint8_t* dst = sB + stage * C::B_BYTES;
-        for (int i = t; i < BN * 4; i += 128) {
-          const int n = i >> 2;
-          const int c = i & 3;  // 16 int8 along K: k = 16c .. 16c+15
-          const uint4 raw = *reinterpret_cast<const uint4*>(src + n * 64 + c * 16);
+        // BN rows x 64 int8: thread t takes 16-byte chunk c = t & 3 (k = 16c ..
+        // 16c + 15) of rows t / 4 + 32 j; all loads first, then the stores
+        constexpr int NJ = BN * 4 / 128;
+        const int c = t & 3;
+        uint4 raw[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+          raw[j] = lds128(smem_u32(src + ((t >> 2) + 32 * j) * 64 + c * 16));
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const int n = (t >> 2) + 32 * j;
           uint4 o0, o1;
-          i8x4_to_bf16x4(raw.x, o0.x, o0.y);
-          i8x4_to_bf16x4(raw.y, o0.z, o0.w);
-          i8x4_to_bf16x4(raw.z, o1.x, o1.y);
-          i8x4_to_bf16x4(raw.w, o1.z, o1.w);
-          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c)) = o0;
-          *reinterpret_cast<uint4*>(dst + sw128_off(n, 2 * c + 1)) = o1;
+          i8x4_to_bf16x4(raw[j].x, o0.x, o0.y);
+          i8x4_to_bf16x4(raw[j].y, o0.z, o0.w);
+          i8x4_to_bf16x4(raw[j].z, o1.x, o1.y);
+          i8x4_to_bf16x4(raw[j].w, o1.z, o1.w);
+          sts128(smem_u32(dst + sw128_off(n, 2 * c)), o0);
+          sts128(smem_u32(dst + sw128_off(n, 2 * c + 1)), o1);
         }
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
@@ -701,49 +749,55 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
       }
     }
   } else if (C::RMS) {
-    // ── RMSNorm of A (4 warps): thread t owns row t of every A tile. It scales
-    // the row's 64 values of each stage by gamma in place (bf16, the layout
-    // the MMA reads), sums their squares, and at the end of the tile's K loop
-    // hands the row's 1 / sqrt(sum / K + eps) to the epilogue. ──
-    const int t = threadIdx.x - 32 * C::NORM_WARP0;
-    {
-      // gamma over K, zero past K (the TMA zero-fills A past K as well)
-      __nv_bfloat16* g = reinterpret_cast<__nv_bfloat16*>(sGam);
-      const int kpad = p.num_k_blocks * BK;
-      for (int k = t; k < kpad; k += 128)
-        g[k] = k < p.K ? p.rms_gamma[k] : __float2bfloat16_rn(0.f);
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four norm warps only
-    }
+    // ── RMSNorm of A (RMS_WARPS warps): RMS_SPLIT threads per row of the A
+    // tile, each taking 8 / RMS_SPLIT of the row's 16-byte chunks in every
+    // stage. A thread scales its values by gamma in place (bf16, the layout
+    // the MMA reads) and sums their squares; at the end of the tile's K loop
+    // the parts go to the epilogue, which forms 1 / sqrt(sum / K + eps). ──
+    constexpr int CPT = 8 / C::RMS_SPLIT;  // chunks per thread per stage
+    const int tt = threadIdx.x - 32 * C::NORM_WARP0;
+    const int t = tt % BM;         // row
+    const int c0 = (tt / BM) * CPT;  // first chunk
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     for (int tile = tile0; tile < num_tiles && ok; tile += tstep) {
-      float ss0 = 0.f, ss1 = 0.f;
+      unsigned long long ss = f2pk(0.f, 0.f);
       for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort_flag, 13)) {
+        if (!mbar_wait_park(&full[stage], phase, abort_flag, 13)) {
           ok = false;
           break;
         }
-        uint8_t* rowp = sA + stage * C::A_BYTES + t * 128;
-        const uint4* gk = reinterpret_cast<const uint4*>(sGam + kb * (BK * 2));
+        const uint32_t rowp = smem_u32(sA + stage * C::A_BYTES + t * 128);
+        const int k0 = kb * BK;
+        uint4 xs[CPT], gs[CPT];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4* q = reinterpret_cast<uint4*>(rowp + ((c ^ (t & 7)) << 4));
-          const uint4 x = *q;
-          const uint4 gv = gk[c];  // (the same address for every lane: a broadcast)
-          const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        for (int i = 0; i < CPT; ++i) {
+          const int c = c0 + i;
+          xs[i] = lds128(rowp + ((c ^ (t & 7)) << 4));
+          // gamma of these 8 columns (one address for every lane); past K (a
+          // multiple of 8) the tile holds zeros and stays zero
+          gs[i] = k0 + c * 8 < p.K
+                      ? __ldg(reinterpret_cast<const uint4*>(p.rms_gamma + k0 + c * 8))
+                      : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+          const int c = c0 + i;
+          const uint32_t xw[4] = {xs[i].x, xs[i].y, xs[i].z, xs[i].w};
+          const uint32_t gw[4] = {gs[i].x, gs[i].y, gs[i].z, gs[i].w};
           uint32_t yw[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float a0 = bf16_lo(xw[j]), a1 = bf16_hi(xw[j]);
-            ss0 = fmaf(a0, a0, ss0);
-            ss1 = fmaf(a1, a1, ss1);
-            yw[j] = cvt_bf16x2(a0 * bf16_lo(gw[j]), a1 * bf16_hi(gw[j]));
+            const unsigned long long a = f2pk(bf16_lo(xw[j]), bf16_hi(xw[j]));
+            ss = ffma2(a, a, ss);
+            float y0, y1;
+            f2up(fmul2(a, f2pk(bf16_lo(gw[j]), bf16_hi(gw[j]))), y0, y1);
+            yw[j] = cvt_bf16x2(y0, y1);
           }
-          *q = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+          sts128(rowp + ((c ^ (t & 7)) << 4), make_uint4(yw[0], yw[1], yw[2], yw[3]));
         }
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
@@ -753,8 +807,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
         }
       }
       if (!ok) break;
-      if (!mbar_wait(&rempty[acc], acc_phase ^ 1, abort_flag, 14)) break;
-      sRstd[acc * BM + t] = 1.0f / sqrtf((ss0 + ss1) / (float)p.K + p.norm_eps);
+      if (!mbar_wait_park(&rempty[acc], acc_phase ^ 1, abort_flag, 14)) break;
+      float s0, s1;
+      f2up(ss, s0, s1);
+      sRstd[(acc * C::RMS_SPLIT + tt / BM) * BM + t] = s0 + s1;
       mbar_arrive(&rfull[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
@@ -782,6 +838,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
                 const CUtensorMap& ty2, const CUtensorMap& tr, const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<BN, WMODE, FUSE, EPI, PAIR>;
   static_assert(C::SMEM_BYTES <= 232448, "GEMM smem budget");
+  static_assert(!C::LN || C::EPI_COLS % 64 == 0, "FUSE_LN: whole 64-column boxes per warp");
   static_assert(!C::LN || C::EPI_GROUPS == 2 || C::EPI_GROUPS == 4,
                 "FUSE_LN: two or four column slices per CTA");
   auto kern = gemm_tc_kernel<BN, WMODE, EPI, FUSE, PAIR>;
@@ -936,9 +993,9 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
     a.norm_eps = fz->eps;
     fuse = gemm::FUSE_LN;
   } else if (fz != nullptr && fz->rms_gamma != nullptr) {
-    // RMSNorm of A in the GEMM: gamma staged over all of K in shared memory
-    using CR = GemmCfg<256, W_BF16_NK, gemm::FUSE_RMS, CK_EPI_STORE>;
-    if (K > CR::RMS_KMAX || (epi != CK_EPI_STORE && epi != CK_EPI_BIAS))
+    // RMSNorm of A in the GEMM: gamma read 16 bytes at a time
+    if (K % 8 != 0 || (reinterpret_cast<uintptr_t>(fz->rms_gamma) & 15u) != 0 ||
+        (epi != CK_EPI_STORE && epi != CK_EPI_BIAS))
       return CK_ERR_UNSUPPORTED;
     a.rms_gamma = reinterpret_cast<const __nv_bfloat16*>(fz->rms_gamma);
     a.norm_eps = fz->eps;
@@ -970,11 +1027,14 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   CUtensorMap ta, tb, ty, ty2, tr;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BK, BM, 128))
     return CK_ERR_INVALID_ARG;
-  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, 32, 32, 64))
+  // output boxes: 32 x 32 (64B swizzle); FUSE_LN 64 x 32 (128B swizzle)
+  const bool ln = fuse == gemm::FUSE_LN;
+  if (!make_tmap_2d(&ty, Y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldy, ln ? 64 : 32, 32,
+                    ln ? 128 : 64))
     return CK_ERR_INVALID_ARG;
-  if (fuse == gemm::FUSE_LN) {
-    if (!make_tmap_2d(&ty2, fz->ln_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, fz->ln_ld, 32,
-                      32, 64))
+  if (ln) {
+    if (!make_tmap_2d(&ty2, fz->ln_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, fz->ln_ld, 64,
+                      32, 128))
       return CK_ERR_INVALID_ARG;
   } else {
     ty2 = ty;
@@ -984,7 +1044,7 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   a.res_tma = fuse == gemm::FUSE_LN;
   if (a.res_tma) {
     if (!make_tmap_2d(&tr, aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N,
-                      aux_row_mod > 0 ? (uint64_t)aux_row_mod : (uint64_t)M, ld_aux, 32, 32, 64))
+                      aux_row_mod > 0 ? (uint64_t)aux_row_mod : (uint64_t)M, ld_aux, 64, 32, 128))
       return CK_ERR_INVALID_ARG;
   } else {
     tr = ty;

@@ -76,8 +76,8 @@ struct GemmFusion {
   // (model weights inside the forward): its first tiles may load before the
   // GEMM's dependency wait
   bool w_static = false;
-  // RMSNorm of A fused into the GEMM (bf16 A, K <= 4096, store or bias
-  // epilogue): y = epi((x * gamma) W^T * (1 / sqrt(mean_k(x^2) + eps)))
+  // RMSNorm of A fused into the GEMM (bf16 A, K a multiple of 8, gamma 16-byte
+  // aligned, store or bias epilogue): y = epi((x * gamma) W^T / sqrt(mean_k(x^2) + eps))
   const void* rms_gamma = nullptr;
 };
 // Tensor-core GEMM when supported, else the CUDA-core one (capi.cu).
@@ -89,7 +89,7 @@ int linear_dispatch(const void* A, int dtype, int64_t M, int64_t K, int64_t lda,
                     int epi, const void* aux, int64_t ld_aux, int64_t aux_row_mod, void* Y,
                     int64_t ldy, cudaStream_t st, bool w_static = false);
 // Norm then linear (capi.cu). RMSNorm over bf16 rows that the tcgen05 GEMM
-// takes (K <= 4096, store or bias epilogue) runs as one launch with the norm
+// takes (K a multiple of 8, store or bias epilogue) runs as one launch with the norm
 // inside the GEMM (norm_linear_fused); every other case writes the normalised
 // rows to the workspace (M * K elements of dtype) and runs the linear after
 // it, and returns CK_ERR_WORKSPACE without launching when that is too small.

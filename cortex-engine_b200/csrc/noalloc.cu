@@ -2,7 +2,7 @@
 // cannot allocate device memory.
 //
 // ck_norm_linear asks its caller for a scratch buffer whenever the call takes
-// the two-launch path (a LayerNorm, fp32 rows, K > 4096, or a GELU / residual
+// the two-launch path (a LayerNorm, fp32 rows, K not a multiple of 8, or a GELU / residual
 // epilogue: the normalised rows go to the buffer, then the linear reads them).
 // Some callers have no device allocator to get that buffer from: a service
 // binding this C ABI from Go, Java or another host runtime without CUDA memory

@@ -135,7 +135,7 @@ int ck_linear(const void* A, int dtype, int64_t M, int64_t K, int64_t lda, const
 /* Norm then linear: replaces rms_norm_linear (cortex/kernels/fused_rmsnorm.py:239-301)
  * with norm_mode = CK_NORM_RMS, and LayerNorm->Linear pairs of the model with
  * CK_NORM_LAYER. RMSNorm of bf16 rows runs as ONE launch when the tensor-core
- * GEMM takes the shapes (16-byte aligned rows, K <= 4096) and the epilogue is
+ * GEMM takes the shapes (16-byte aligned rows and gamma, K a multiple of 8) and the epilogue is
  * CK_EPI_STORE or CK_EPI_BIAS: the GEMM scales every A tile by gamma in shared
  * memory, sums x^2 per row on the way, and multiplies each output row by
  * 1 / sqrt(sum / K + eps) in its epilogue, so x is read once and no normalised

@@ -398,7 +398,7 @@ def _norm_linear_call(x, g, w, sc, bias, ws=None):
 
 
 @pytest.mark.parametrize("M,K,N", [(8192, 512, 1536), (8192, 512, 2048), (1000, 768, 256),
-                                   (130, 4096, 384), (64, 64, 128)])
+                                   (130, 4096, 384), (64, 64, 128), (256, 6144, 256)])
 @pytest.mark.parametrize("wkind", ["bf16", "int8"])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_norm_linear_fused_single_launch(M, K, N, wkind, with_bias):

@@ -94,6 +94,49 @@ def test_cfg3_full_batch_matches_oracle():
     assert _rel(y["behavior"], ref) <= TOL["bfloat16"]
 
 
+def _pick_windows(inp, counts, picks):
+    """The events of windows ``picks`` (in that order), batch indices rebased."""
+    off = np.concatenate([[0], np.cumsum(counts)])
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    out = {k: [] for k in cols}
+    for j, b in enumerate(picks):
+        e0, e1 = int(off[b]), int(off[b + 1])
+        for k in cols[:3]:
+            out[k].append(inp[k][e0:e1])
+        out["batch_indices"].append(torch.full((e1 - e0,), j, dtype=torch.int64))
+    return [torch.cat(out[k]) for k in cols]
+
+
+def test_cfg4_micro_batch_matches_oracle():
+    """Cortex-M variant with INT8 weights (cfg4) at the bench's micro-batch of
+    256 windows x 1024 events: six windows spread over the batch match the
+    oracle evaluated in bf16 and in fp32 within the cfg4 bound, max(2e-2, 1.25 x
+    the bf16 oracle's own distance from fp32); the first and the last window
+    are bit-identical when decoded alone."""
+    from cortex.workloads import make_inputs
+
+    wl, model = _model("cfg4")
+    inp, counts = make_inputs(wl, seed=3, batch=256)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        y = model(*(inp[k].to(DEV) for k in cols))["behavior"]
+        picks = [0, 51, 102, 153, 204, 255]
+        alone = [model(*(t.to(DEV) for t in _pick_windows(inp, counts, [b])))["behavior"]
+                 for b in (0, 255)]
+    assert y.shape == (256, 2) and torch.isfinite(y).all()
+    assert torch.equal(alone[0][0], y[0]) and torch.equal(alone[1][0], y[255])
+    sub = _pick_windows(inp, counts, picks)
+    torch.set_num_threads(max(torch.get_num_threads(), 8))
+    p16 = {k: v.cpu() for k, v in model.state_dict().items()}
+    p32 = {k: (v.float() if v.is_floating_point() else v) for k, v in p16.items()}
+    ref16 = O.forward(p16, wl.config, *sub).float()
+    ref32 = O.forward(p32, wl.config, *sub).float()
+    tol = max(TOL["bfloat16"], 1.25 * _rel(ref16, ref32))
+    got = y[picks]
+    assert _rel(got, ref16) <= tol, (_rel(got, ref16), tol)
+    assert _rel(got, ref32) <= tol, (_rel(got, ref32), tol)
+
+
 @pytest.mark.parametrize("name", ["cfg1", "cfg3"])
 def test_windows_are_independent(name):
     """Result of window b is bit-identical whether it runs alone or in the batch."""

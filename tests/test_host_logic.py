@@ -192,16 +192,24 @@ def test_int8_workload_converts_exactly_the_self_attention_linears():
 
 
 def test_int8_to_bf16_bit_trick_is_exact_for_every_byte():
-    """The GEMM widens int8 weight tiles to bf16 with byte permutes and one fp32
-    subtraction (i8x4_to_bf16x4 in csrc/common.cuh): byte b ^ 0x80 in the low
-    byte of the fp32 word 0x4B000000 is 2^23 + 128 + v; minus (2^23 + 128) it is
-    v, and the upper 16 bits of that fp32 are bf16(v). Restated in numpy for all
-    256 byte values against torch's own int8 -> bf16 conversion."""
+    """The GEMM widens int8 weight tiles to bf16 with integer logic and one
+    bf16x2 subtraction (i8x4_to_bf16x4 in csrc/common.cuh): the bf16 with bits
+    0x4300 | (v & 0x7F) minus the bf16 0x4300 | (v & 0x80) is v. Restated in
+    numpy for all 256 byte values (the byte order of the packed words too)
+    against torch's own int8 -> bf16 conversion."""
     v = np.arange(-128, 128, dtype=np.int8)
-    u = (v.view(np.uint8) ^ 0x80).astype(np.uint32)
-    word = (0x4B000000 | u).astype(np.uint32)
-    f = word.view(np.float32) - np.float32(8388736.0)
-    assert np.array_equal(f, v.astype(np.float32))
-    bf = (f.view(np.uint32) >> 16).astype(np.uint16)
+    u = v.view(np.uint8).astype(np.uint32)
+    x = (0x4300 | (u & 0x7F)).astype(np.uint32) << 16  # bf16 bits as the top of an fp32
+    s_ = (0x4300 | (u & 0x80)).astype(np.uint32) << 16
+    diff = x.view(np.float32) - s_.view(np.float32)  # exact: integers of magnitude <= 256
+    assert np.array_equal(diff, v.astype(np.float32))
+    got = (diff.view(np.uint32) >> 16).astype(np.uint16)
     ref = torch.from_numpy(v.copy()).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
-    assert np.array_equal(bf, ref)
+    assert np.array_equal(got, ref)
+    # the byte permute (b0, b2, b1, b3): even 16-bit lanes then hold (b0, b1),
+    # odd ones (b2, b3), the order of the bf16 pairs written out
+    w = np.uint32(0x44332211)
+    b = [(int(w) >> (8 * i)) & 0xFF for i in range(4)]
+    r = b[0] | (b[2] << 8) | (b[1] << 16) | (b[3] << 24)
+    assert (r & 0xFF, (r >> 16) & 0xFF) == (b[0], b[1])
+    assert ((r >> 8) & 0xFF, (r >> 24) & 0xFF) == (b[2], b[3])
