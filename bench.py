@@ -63,9 +63,16 @@ UNIT = "windows/s"
 # DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum) of
 # the kernel classes captured on B200, keyed by (config, class); see profiles/.
 NCU_TRAFFIC = {
-    ("cfg1", "gemm_resid"): {"bytes": 28_900_000, "note": "mean of the forward's 14 launches "
-                             "with the fused LayerNorm: out_proj 17.4 MB, mlp.2 44.3 MB "
+    ("cfg1", "gemm_resid"): {"bytes": 28_900_000, "note": "mean over the forward's 14 launches "
+                             "with the fused LayerNorm, the cross out_proj counted like an "
+                             "out_proj: out_proj 17.4 MB, mlp.2 44.1 MB "
                              "(profiles/gemm_tc_resid_ln_cfg1.md)"},
+    ("cfg1", "gemm_gelu"): {"bytes": 10_580_000, "note": "layer 0's mlp.0 "
+                            "(profiles/gemm_tc_mlp0_gelu_cfg1.md)"},
+    ("cfg1", "attention"): {"bytes": 25_390_000, "note": "layer 0's self-attention "
+                            "(profiles/attn_ws_self_cfg1.md)"},
+    ("cfg2", "gemm_store"): {"bytes": 9_230_000, "note": "layer 0's INT8 qkv_proj "
+                             "(profiles/gemm_tc_int8_qkv_cfg2.md)"},
 }
 
 
@@ -612,6 +619,114 @@ class Decoder:
         self.graphs = None
 
 
+# The reference's own benchmark of its fused RMSNorm + linear (Triton), bf16 on
+# an NVIDIA A10 (benchmarks/kernels/fused_rmsnorm.json): (M, K, N) -> ms.
+REF_RMS_A10_MS = {(256, 512, 1536): 0.0926, (256, 512, 2048): 0.0932,
+                  (8192, 512, 1536): 0.6976, (8192, 512, 2048): 0.8796,
+                  (8192, 256, 768): 0.1982, (8192, 512, 512): 0.2438}
+
+
+def norm_linear_block(dev, st, flush, reps: int = 50):
+    """rms_norm_linear at the reference benchmark's shapes: the one-launch
+    kernel (ck_norm_linear, RMS, bf16, W (K, N) as the reference passes it, and
+    the INT8-weight variant), the two-launch path beside it (ck_row_norm, then
+    ck_linear), each launch alone in a graph replay after an L2 flush."""
+    import torch
+
+    from cortex import _lib as L
+
+    lib = L.load()
+    hbm, tf_burst, _, kind = peaks()
+    out = []
+    for (M, K, N), ref_ms in REF_RMS_A10_MS.items():
+        torch.manual_seed(0)
+        x = torch.randn(M, K, dtype=torch.bfloat16, device=dev)
+        g = (torch.rand(K, device=dev) + 0.5).to(torch.bfloat16)
+        w = torch.randn(K, N, dtype=torch.bfloat16, device=dev)
+        w8 = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+        sc = torch.rand(N, device=dev) * 1e-2
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        xn = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+
+        def fused():
+            L.check(lib.ck_norm_linear(x.data_ptr(), L.CK_BF16, M, K, K, g.data_ptr(), None, 1e-6,
+                                       L.CK_NORM_RMS, w.data_ptr(), L.CK_BF16, L.CK_W_KN, N, N,
+                                       None, L.CK_EPI_STORE, None, 0, 0, y.data_ptr(), N, None, 0,
+                                       L.stream_of(dev)), "ck_norm_linear")
+
+        def fused_int8():
+            L.check(lib.ck_norm_linear(x.data_ptr(), L.CK_BF16, M, K, K, g.data_ptr(), None, 1e-6,
+                                       L.CK_NORM_RMS, w8.data_ptr(), L.CK_I8, L.CK_W_NK, N, K,
+                                       sc.data_ptr(), L.CK_EPI_STORE, None, 0, 0, y.data_ptr(), N,
+                                       None, 0, L.stream_of(dev)), "ck_norm_linear int8")
+
+        def two_launch():
+            s_ = L.stream_of(dev)
+            L.check(lib.ck_row_norm(x.data_ptr(), L.CK_BF16, M, K, K, g.data_ptr(), None, 1e-6,
+                                    L.CK_NORM_RMS, xn.data_ptr(), K, s_), "ck_row_norm")
+            L.check(lib.ck_linear(xn.data_ptr(), L.CK_BF16, M, K, K, w.data_ptr(), L.CK_BF16,
+                                  L.CK_W_KN, N, N, None, L.CK_EPI_STORE, None, 0, 0, y.data_ptr(),
+                                  N, s_), "ck_linear")
+
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            ts = time_steps(st, flush, gr.replay, reps)
+            del gr
+            return sum(ts) / len(ts)
+
+        t1, t8, t2 = timed(fused), timed(fused_int8), timed(two_launch)
+        fl = 2.0 * M * N * K
+        out.append({"M": M, "K": K, "N": N, "one_launch_us": round(t1 * 1e6, 2),
+                    "one_launch_tflops": round(fl / t1 / 1e12, 1),
+                    "frac": round(fl / t1 / 1e12 / tf_burst, 4),
+                    "int8_weights_us": round(t8 * 1e6, 2),
+                    "two_launch_us": round(t2 * 1e6, 2),
+                    "reference_a10_triton_ms": ref_ms,
+                    "vs_reference_a10": round(ref_ms * 1e-3 / t1, 1)})
+    return {"what": "rms_norm_linear (RMSNorm in the tcgen05 GEMM's A prologue, 1/rms in its "
+                    "epilogue) at the shapes of the reference's kernel benchmark, bf16, W (K, N); "
+                    "mean of " + str(reps) + " launches, each alone in a graph replay after an "
+                    "L2 flush, CUDA events on the stream",
+            "peak_kind": f"{kind} bf16 burst {tf_burst} TFLOP/s",
+            "reference": "benchmarks/kernels/fused_rmsnorm.json (NVIDIA A10, Triton)",
+            "shapes": out}
+
+
+def only_kernel(args):
+    """A few launches of one kernel (for ncu): the fused RMSNorm + linear at
+    8192 x 512 x 1536 (bf16 W (K, N), or int8 W with --only-kernel rms_int8)."""
+    import torch
+
+    sys.path.insert(0, PKG)
+    from cortex import _lib as L
+
+    lib = L.load()
+    dev = torch.device("cuda", 0)
+    M, K, N = 8192, 512, 1536
+    torch.manual_seed(0)
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=dev)
+    g = (torch.rand(K, device=dev) + 0.5).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    if args.only_kernel == "rms_int8":
+        w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+        sc = torch.rand(N, device=dev) * 1e-2
+        wa = (w.data_ptr(), L.CK_I8, L.CK_W_NK, N, K, sc.data_ptr())
+    else:
+        w = torch.randn(K, N, dtype=torch.bfloat16, device=dev)
+        wa = (w.data_ptr(), L.CK_BF16, L.CK_W_KN, N, N, None)
+    for _ in range(3):
+        L.check(lib.ck_norm_linear(x.data_ptr(), L.CK_BF16, M, K, K, g.data_ptr(), None, 1e-6,
+                                   L.CK_NORM_RMS, *wa, L.CK_EPI_STORE, None, 0, 0, y.data_ptr(),
+                                   N, None, 0, L.stream_of(dev)), "ck_norm_linear")
+    torch.cuda.synchronize()
+    L.check_device_status("only-kernel")
+    print(json.dumps({"only_kernel": args.only_kernel, "M": M, "K": K, "N": N, "launches": 3}))
+
+
 def time_steps(st, flush, fn, steps):
     import torch
 
@@ -847,6 +962,10 @@ def run_ours(args):
             except Exception as e:  # report, do not sink the headline line
                 cfgs[name] = {"error": f"{type(e).__name__}: {e}"}
         line["configs"] = cfgs
+        try:
+            line["norm_linear"] = norm_linear_block(dev, st, flush)
+        except Exception as e:
+            line["norm_linear"] = {"error": f"{type(e).__name__}: {e}"}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, wl.name)
     print(json.dumps(line), flush=True)
@@ -870,8 +989,12 @@ def main():
                     help="time the forwards only (no e2e / roofline / CPU legs); for ncu runs")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--cpu-sample", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--only-kernel", choices=["rms", "rms_int8"], default=None,
+                    help="launch one kernel a few times and exit (for ncu)")
     args = ap.parse_args()
-    if args.cpu_sample:
+    if args.only_kernel:
+        only_kernel(args)
+    elif args.cpu_sample:
         cpu_sample_main(args)
     elif args.impl == "reference":
         run_reference(args)
