@@ -6,22 +6,32 @@
 // Two persistent CTAs per SM walk the (batch, head, 128-query tile) work items
 // with a stride of the grid. Each CTA runs one in-order pipeline over the
 // 128-key chunks of its items:
-//   warp 4   TMA producer: the item's Q tile, then K and V of every chunk into
+//   warp 8   TMA producer: the item's Q tile, then K and V of every chunk into
 //            a two-stage ring (the next item's loads start while the current
 //            item is still in its softmax)
-//   warp 5   TMEM owner and MMA issuer:
-//              S_g = Q K_g^T    M=128 N=128 K=64  -> TMEM cols [0,128)
-//              O  += P_g V_g    M=128 N=64  K=128 -> TMEM cols [128,192)
+//   warp 9   TMEM owner and MMA issuer:
+//              S_g   = Q K_g^T          M=128 N=128 K=64 -> TMEM cols [0,128)
+//              O_h  += P_g,h V_g,h      M=128 N=64  K=64 -> TMEM cols [128+64h, +64)
+//            for the two key halves h (keys 64h .. 64h+63 of the chunk).
 //            S_{g+1} is issued as soon as the softmax has read S_g, so the next
 //            product runs under the current chunk's softmax
-//   warps 0-3 softmax, thread r = query row r = TMEM lane r: 128 scores per
-//            chunk from TMEM, row max, exp2, row sum, P (bf16) into a
-//            128B-swizzled smem operand; an item's O / l goes to global once
-//            the next item's first chunk is exponentiated (or at the end)
-// The output accumulates in TMEM across chunks. The softmax keeps a running
-// base m per row and rescales O (in TMEM) only when a chunk's maximum exceeds
-// m by more than 2^8; otherwise P = exp2(s - m) <= 256 is used as is, which
-// is exact in real arithmetic after the final O / l. All waits are bounded.
+//   warps 0-7 softmax, two warps per TMEM lane quarter: warp w takes query
+//            row r = 32 (w % 4) + lane and key half h = w / 4 of every chunk:
+//            its 64 scores from TMEM, its own running max and row sum, exp2,
+//            and the 64-key atom h of P (bf16, 128B-swizzled smem operand).
+//            The halves are two independent online softmaxes with their own
+//            accumulators O_0, O_1, so the two warps of a row never wait for
+//            each other inside an item. Two warps per row halve each thread's
+//            dependent chain and give every scheduler four softmax warps (two
+//            CTAs per SM) to hide its latencies with.
+// An item's output is written once the next item's first chunk has been
+// exponentiated (or at the end): half 1 divides O_1 by its row sum in TMEM and
+// publishes its log2-sum-exp c_1 = m_1 + log2 l_1; half 0 combines
+//   O = (O_0 / l_0) w_0 + (O_1 / l_1) w_1,  w_h = 2^c_h / (2^c_0 + 2^c_1),
+// and writes the row. Each half keeps a running base m and rescales its O_h
+// (in TMEM) only when a chunk's maximum exceeds m by more than 2^8; otherwise
+// P = exp2(s - m) <= 256 is used as is, which is exact in real arithmetic after
+// the final division. All waits are bounded.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -38,14 +48,18 @@ constexpr int Q_BYTES = QT * DH * 2;    // 16 KB
 constexpr int KV_BYTES = KC * DH * 2;   // 16 KB: one K or one V chunk
 constexpr int P_BYTES = QT * KC * 2;    // 32 KB: two 128B-swizzled atoms
 constexpr int STAGES = 2;               // K/V ring
-constexpr int NTHREADS = 192;           // softmax warps 0-3, producer warp 4, MMA warp 5
+constexpr int NTHREADS = 320;           // softmax warps 0-7, producer warp 8, MMA warp 9
+constexpr int NSOFT = 256;              // softmax threads: two per query row
 constexpr int BAR_BYTES = 256;
+constexpr int XCH_BYTES = QT * 4;       // c_1 of every row, from key half 1 to half 0
 constexpr int CTAS_PER_SM = 2;          // 2 x (SMEM_BYTES + 1 KB) <= 228 KB; 2 x 256 TMEM cols
-constexpr int SMEM_BYTES = Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + BAR_BYTES;
-constexpr uint32_t TMEM_COLS = 256;     // S [0, 128), O [128, 192)
+constexpr int SMEM_BYTES = Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + XCH_BYTES + BAR_BYTES;
+constexpr uint32_t TMEM_COLS = 256;     // S [0, 128), O_0 [128, 192), O_1 [192, 256)
+constexpr int KH = KC / 2;              // keys per half chunk
 constexpr uint32_t IDESC_S = idesc_bf16(128, KC, 0);
 constexpr uint32_t IDESC_O = idesc_bf16(128, DH, 1);
 constexpr float kRescaleLog2 = 8.f;
+static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two CTAs per SM");
 
 struct WsArgs {
   int B, H, Lq, n_keys, num_q_tiles, num_items;
@@ -97,6 +111,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 16 consecutive fp32 TMEM columns of this thread's lane, and the store back.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
@@ -140,7 +160,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
   uint8_t* sQ = smem_raw;
   uint8_t* sKV = sQ + Q_BYTES;  // [STAGES][K chunk | V chunk]
   uint8_t* sP = sKV + STAGES * 2 * KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  float* xlse = reinterpret_cast<float*>(sP + P_BYTES);  // [QT]: c_1 per row
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES + XCH_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;    // [STAGES]
@@ -148,11 +169,12 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
   uint64_t* kv_empty = bars + 6;  // [STAGES]
   uint64_t* s_full = bars + 8;
   uint64_t* s_free = bars + 9;
-  uint64_t* p_full = bars + 10;
-  uint64_t* o_full = bars + 11;
-  uint64_t* o_free = bars + 12;
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* p_full = bars + 10;   // [2 key halves]
+  uint64_t* o_full = bars + 12;   // [2 key halves]
+  uint64_t* o_free = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint64_t* x_ready = bars + 16;  // [4 lane quarters]: half 1 published c_1, O_1 / l_1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -168,16 +190,19 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, 128);
+    mbar_init(s_free, NSOFT);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&p_full[h], NSOFT / 2);
+      mbar_init(&o_full[h], 1);
+    }
+    mbar_init(o_free, NSOFT);
     mbar_init(drain, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&x_ready[q], 32);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -190,7 +215,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
   const uint32_t tmem_s = tmem_base;
   const uint32_t tmem_o = tmem_base + 128;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ── TMA producer ──
     if (lane == 0) {
       int g = 0, nq = 0;
@@ -225,7 +250,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
           mbar_wait(&v_full[st], (uint32_t)((kv_loads[st] - 1) & 1), nullptr, 43);
         }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ── MMA issuer ──
     if (lane == 0) {
       int g = 0, nq = 0;
@@ -235,22 +260,24 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
       bool ok = true;
       auto issue_pv = [&]() -> bool {
         const int st = pv_g & 1;
-        if (!mbar_wait(p_full, (uint32_t)(pv_g & 1), abort_flag, 44)) return false;
         if (!mbar_wait(&v_full[st], (uint32_t)((pv_g >> 1) & 1), abort_flag, 45)) return false;
-        // the item's first product overwrites O: the previous item's O is read
+        // the item's first products overwrite O_0, O_1: the previous item's are read
         if (pv_j == 0 && pv_item > 0 &&
             !mbar_wait(o_free, (uint32_t)((pv_item - 1) & 1), abort_flag, 46))
           return false;
-        tc_fence_after();
         const uint32_t pa = smem_u32(sP), va = smem_u32(sKV + st * 2 * KV_BYTES + KV_BYTES);
+        for (int h = 0; h < 2; ++h) {  // each half's product once its P atom is in
+          if (!mbar_wait(&p_full[h], (uint32_t)(pv_g & 1), abort_flag, 44)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < KC / 16; ++k) {
-          const uint64_t adesc = sw128_desc(pa + (k >> 2) * (QT * 128) + (k & 3) * 32, 16, 1024);
-          const uint64_t bdesc = sw128_desc(va + k * 16 * 128, 8192, 1024);
-          tc_mma_ss(tmem_o, adesc, bdesc, IDESC_O, (pv_j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 4 * h; k < 4 * h + 4; ++k) {
+            const uint64_t adesc = sw128_desc(pa + h * (QT * 128) + (k & 3) * 32, 16, 1024);
+            const uint64_t bdesc = sw128_desc(va + k * 16 * 128, 8192, 1024);
+            tc_mma_ss(tmem_o + 64 * h, adesc, bdesc, IDESC_O, (pv_j > 0 || k > 4 * h) ? 1u : 0u);
+          }
+          tc_commit(&o_full[h]);
         }
         tc_commit(&kv_empty[st]);
-        tc_commit(o_full);
         return true;
       };
       for (int w = blockIdx.x; w < p.num_items && ok; w += gridDim.x) {
@@ -287,36 +314,68 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
       mbar_wait(drain, 0, nullptr, 50);
     }
   } else {
-    // ── softmax: thread r owns query row r ──
-    // An item's epilogue (O / l to global) runs after the next item's first
-    // chunk has been exponentiated, so the last P V product of the item
-    // completes under that softmax instead of stalling the warp.
-    const int row = tid;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    int g = 0;
+    // ── softmax: two warps per query row, each one key half of every chunk ──
+    // An item's output is written after the next item's first chunk has been
+    // exponentiated, so the last P V products of the item complete under that
+    // softmax instead of stalling the warps.
+    const int quarter = warp & 3;  // TMEM lane quarter
+    const int kh = warp >> 2;      // key half
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tmem_oh = tmem_o + lane_off + 64 * kh;
+    int g = 0, nout = 0;
     bool ok = true;
-    bool pend = false;  // an item whose O has not been written out yet
-    float pend_l = 0.f;
+    bool pend = false;  // an item whose output has not been written yet
+    float pend_m = 0.f, pend_l = 0.f;
     __nv_bfloat16* pend_dst = nullptr;
-    auto epilogue = [&]() {  // 16 columns at a time: the caller still holds P
+    // Runs after o_full[kh] of the item's last chunk. Half 1 normalises O_1
+    // in TMEM and publishes c_1; half 0 waits for that and writes the row.
+    auto epilogue = [&]() -> bool {
       __syncwarp();
       tc_fence_after();
       const float inv = (pend_l > 0.f) ? 1.f / pend_l : 0.f;
-#pragma unroll
-      for (int q = 0; q < DH / 16; ++q) {
-        float ov[16];
-        tmem_ld16(tmem_o + lane_off + q * 16, ov);
+      const float c = (pend_l > 0.f) ? pend_m + lg2(pend_l) : -INFINITY;
+      if (kh == 1) {  // the whole row in one TMEM round trip
+        float ov[DH];
+        tmem_ld32(tmem_oh, ov);
+        tmem_ld32(tmem_oh + 32, ov + 32);
         tc_wait_ld();
-        if (pend_dst != nullptr) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) ov[i] *= inv;
-          reinterpret_cast<uint4*>(pend_dst)[2 * q] = pack8(ov);
-          reinterpret_cast<uint4*>(pend_dst)[2 * q + 1] = pack8(ov + 8);
+        for (int i = 0; i < DH; ++i) ov[i] *= inv;
+#pragma unroll
+        for (int q = 0; q < DH / 16; ++q) tmem_st16(tmem_oh + q * 16, ov + 16 * q);
+        tc_wait_st();
+        xlse[row] = c;
+        tc_fence_before();
+        mbar_arrive(&x_ready[quarter]);
+      } else {
+        if (!mbar_wait(&x_ready[quarter], (uint32_t)(nout & 1), abort_flag, 54)) return false;
+        tc_fence_after();
+        const float c1 = xlse[row];
+        const float mx = fmaxf(c, c1);  // c (half 0) is finite: the item has keys
+        const float e0 = ex2(c - mx), e1 = ex2(c1 - mx);
+        const float rt = 1.f / (e0 + e1);
+        const float f0 = e0 * rt * inv, f1 = e1 * rt;
+#pragma unroll
+        for (int q = 0; q < DH / 32; ++q) {  // 32 columns of O_0 and O_1 per round trip
+          float o0[32], o1[32];
+          tmem_ld32(tmem_oh + q * 32, o0);
+          tmem_ld32(tmem_oh + 64 + q * 32, o1);
+          tc_wait_ld();
+          if (pend_dst != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o0[i] = fmaf(o0[i], f0, o1[i] * f1);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              reinterpret_cast<uint4*>(pend_dst)[4 * q + c] = pack8(o0 + 8 * c);
+          }
         }
+        tc_fence_before();
       }
-      tc_fence_before();
-      mbar_arrive(o_free);  // O may be overwritten by the next item's first P V
+      mbar_arrive(o_free);  // O_0, O_1 may be overwritten by the next item
+      ++nout;
       pend = false;
+      return true;
     };
     for (int w = blockIdx.x; w < p.num_items && ok; w += gridDim.x) {
       const Item it = make_item(p, w);
@@ -328,10 +387,12 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
       if (it.nch == 0) {  // no keys: attention over nothing is 0
         if (l < p.Lq)
 #pragma unroll
-          for (int c = 0; c < DH / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < DH / 16; ++c)
+            reinterpret_cast<uint4*>(dst + kh * (DH / 2))[c] = make_uint4(0, 0, 0, 0);
         continue;
       }
       float m_run = 0.f, l_run = 0.f;
+      bool have = false;  // a valid key of this half seen in this item
       for (int j = 0; j < it.nch; ++j, ++g) {
         if (!mbar_wait(s_full, (uint32_t)(g & 1), abort_flag, 51)) {
           ok = false;
@@ -339,86 +400,104 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         }
         __syncwarp();
         tc_fence_after();
-        float s[KC];
+        float s[KH];
 #pragma unroll
-        for (int q = 0; q < KC / 32; ++q) tmem_ld32(tmem_s + lane_off + q * 32, s + 32 * q);
+        for (int q = 0; q < KH / 32; ++q)
+          tmem_ld32(tmem_s + lane_off + kh * KH + q * 32, s + 32 * q);
         tc_wait_ld();
         tc_fence_before();
         mbar_arrive(s_free);  // S may be overwritten by the next product
-        const int lim = it.nk - j * KC;
-        if (lim < KC) {
+        const int lim = it.nk - j * KC - kh * KH;  // valid keys in this half
+        if (lim < KH) {
 #pragma unroll
-          for (int c = 0; c < KC; ++c)
+          for (int c = 0; c < KH; ++c)
             if (c >= lim) s[c] = -INFINITY;
         }
-        float t[8];
+        float u[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) t[c] = s[c];
+        for (int c = 0; c < 8; ++c) u[c] = s[c];
 #pragma unroll
-        for (int c = 8; c < KC; ++c) t[c & 7] = fmaxf(t[c & 7], s[c]);
-        const float cmax = fmaxf(fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3])),
-                                 fmaxf(fmaxf(t[4], t[5]), fmaxf(t[6], t[7]))) *
+        for (int c = 8; c < KH; ++c) u[c & 7] = fmaxf(u[c & 7], s[c]);
+        const float cmax = fmaxf(fmaxf(fmaxf(u[0], u[1]), fmaxf(u[2], u[3])),
+                                 fmaxf(fmaxf(u[4], u[5]), fmaxf(u[6], u[7]))) *
                            p.scale_log2;  // scale > 0: max commutes with it
         float alpha = 1.f;
         bool rescale = false;
-        if (j == 0) {
-          m_run = cmax;  // chunk 0 holds at least one key
+        if (!have) {
+          // O_h and l hold zeros so far (every earlier P of this half was 0):
+          // the base can start here without a rescale
+          if (cmax > -INFINITY) {
+            m_run = cmax;
+            have = true;
+          } else {
+            m_run = 0.f;  // no key in this half yet: P = 0
+          }
         } else if (cmax > m_run + kRescaleLog2) {
           alpha = ex2(m_run - cmax);
           m_run = cmax;
           rescale = true;
         }
-#pragma unroll
-        for (int c = 0; c < KC; ++c) s[c] = ex2(fmaf(s[c], p.scale_log2, -m_run));
-#pragma unroll
-        for (int c = 0; c < 8; ++c) t[c] = s[c];
-#pragma unroll
-        for (int c = 8; c < KC; ++c) t[c & 7] += s[c];
-        l_run = l_run * alpha + (((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7])));
-        // P V of the previous chunk is done: P's buffer is free and O holds it
-        if (g > 0 && !mbar_wait(o_full, (uint32_t)((g - 1) & 1), abort_flag, 52)) {
+        // P_h V_h of the previous chunk is done: atom h of P is free and O_h holds it
+        if (g > 0 && !mbar_wait(&o_full[kh], (uint32_t)((g - 1) & 1), abort_flag, 52)) {
           ok = false;
           break;
         }
-        if (pend) epilogue();  // the previous item's O (its last P V just completed)
-        if (__any_sync(0xffffffffu, rescale)) {  // rare: bring O to the new base
+        // exp2 straight into atom h of P (bf16, 128B swizzle), and the row sum
+        uint8_t* patom = sP + kh * (QT * 128);
+        float t[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) t[c] = 0.f;
+#pragma unroll
+        for (int gq = 0; gq < KH / 8; ++gq) {
+          float e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            e[i] = ex2(fmaf(s[8 * gq + i], p.scale_log2, -m_run));
+            t[i] += e[i];
+          }
+          sts128(smem_u32(patom + sw128_off(row, gq)),
+                 make_uint4(cvt_bf16x2(e[0], e[1]), cvt_bf16x2(e[2], e[3]),
+                            cvt_bf16x2(e[4], e[5]), cvt_bf16x2(e[6], e[7])));
+        }
+        l_run = l_run * alpha + (((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7])));
+        if (__any_sync(0xffffffffu, rescale)) {  // rare: bring O_h to the new base
           __syncwarp();
           tc_fence_after();
 #pragma unroll
           for (int q = 0; q < DH / 16; ++q) {
             float ov[16];
-            tmem_ld16(tmem_o + lane_off + q * 16, ov);
+            tmem_ld16(tmem_oh + q * 16, ov);
             tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) ov[i] *= alpha;
-            tmem_st16(tmem_o + lane_off + q * 16, ov);
+            tmem_st16(tmem_oh + q * 16, ov);
           }
           tc_wait_st();
         }
-        // P (bf16, 128B swizzle, keys 0..63 in atom 0, 64..127 in atom 1)
-#pragma unroll
-        for (int gq = 0; gq < KC / 8; ++gq) {
-          *reinterpret_cast<uint4*>(sP + (gq >> 3) * (QT * 128) + sw128_off(row, gq & 7)) =
-              make_uint4(cvt_bf16x2(s[8 * gq], s[8 * gq + 1]), cvt_bf16x2(s[8 * gq + 2], s[8 * gq + 3]),
-                         cvt_bf16x2(s[8 * gq + 4], s[8 * gq + 5]),
-                         cvt_bf16x2(s[8 * gq + 6], s[8 * gq + 7]));
-        }
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[kh]);
+        // the previous item, whose last products completed before this chunk's
+        // P V could start (that product waits for o_free from here)
+        if (pend && !epilogue()) {
+          ok = false;
+          break;
+        }
       }
       if (!ok) break;
       pend = true;
+      pend_m = m_run;
       pend_l = l_run;
       pend_dst = (l < p.Lq) ? dst : nullptr;
     }
-    // the last item's O, once its last P V is done
-    if (ok && pend && mbar_wait(o_full, (uint32_t)((g - 1) & 1), abort_flag, 53)) epilogue();
+    // the last item's output, once its last products are done
+    if (ok && pend && mbar_wait(&o_full[kh], (uint32_t)((g - 1) & 1), abort_flag, 53))
+      epilogue();
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }

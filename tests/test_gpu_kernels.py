@@ -480,7 +480,9 @@ def _qkv(B, H, L, E, Dh, dtype):
 
 @pytest.mark.parametrize("B,H,L,E,Dh", [(1, 1, 32, 64, 16), (2, 4, 64, 128, 32),
                                         (1, 8, 128, 256, 64), (2, 8, 256, 512, 64),
-                                        (3, 2, 200, 77, 64), (1, 2, 130, 1000, 64)])
+                                        (3, 2, 200, 77, 64), (1, 2, 130, 1000, 64),
+                                        (2, 2, 64, 40, 64), (1, 2, 128, 64, 64),
+                                        (1, 2, 128, 129, 64)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_attention_dense(B, H, L, E, Dh, dtype):
     from cortex.kernels.sparse_xattn import sparse_cross_attention
@@ -525,6 +527,66 @@ def test_attention_golden_and_all_masked(golden_kernels):
         z = torch.zeros(2, 4, dtype=torch.bool)
         out = sparse_cross_attention(q.to(DEV), k.to(DEV), v.to(DEV), z, 64, 64)
         assert torch.equal(out.cpu(), torch.zeros_like(q))
+
+
+def _varlen_attention(lens, H, Lq, scale, seed, key_growth=0.0, q_gain=1.0):
+    """Packed-key attention through ck_attention (the warp-specialised tcgen05
+    path: bf16, head_dim 64, no masks) against an fp32 restatement per batch.
+    q, o: (B, Lq, H*64) rows; k, v: the batches' keys packed back to back,
+    (sum(lens), H*64), with int32 key offsets."""
+    from cortex.kernels import _ops
+
+    B, Dh = len(lens), 64
+    g = torch.Generator().manual_seed(seed)
+    nk = int(sum(lens))
+    q = torch.randn(B, Lq, H * Dh, generator=g) * q_gain
+    k = torch.randn(max(nk, 1), H * Dh, generator=g)
+    if key_growth:  # later keys larger: the running max keeps rising
+        k *= 1 + key_growth * torch.arange(k.shape[0]).float()[:, None] / max(nk, 1)
+    v = torch.randn(max(nk, 1), H * Dh, generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    offs = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    o = torch.full((B, Lq, H * Dh), float("nan"), dtype=torch.bfloat16, device=DEV)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    _ops.attention(qd, kd, vd, B=B, H=H, Dh=Dh, Lq=Lq, key_offsets=offs.to(DEV),
+                   q_geom=(H * Dh, B * Lq, Lq, 0, Dh), k_geom=(H * Dh, k.shape[0], 0, 0, Dh),
+                   v_geom=(H * Dh, v.shape[0], 0, 0, Dh), o=o, o_geom=(H * Dh, Lq, 0, Dh),
+                   scale=scale)
+    ref = torch.zeros(B, Lq, H * Dh)
+    for b in range(B):
+        s0, s1 = int(offs[b]), int(offs[b + 1])
+        if s1 == s0:
+            continue
+        for h in range(H):
+            cs = slice(h * Dh, (h + 1) * Dh)
+            sc = (q[b, :, cs].double() @ k[s0:s1, cs].double().T) * scale
+            ref[b, :, cs] = (torch.softmax(sc, -1) @ v[s0:s1, cs].double()).float()
+    return o.float().cpu(), ref
+
+
+@pytest.mark.parametrize("lens", [[0, 1, 63, 64, 65, 300], [127, 128, 129, 0, 256, 2],
+                                  [1000, 17, 0, 0, 513]])
+def test_attention_packed_keys_half_chunk_edges(lens):
+    """Key counts on both sides of the 64-key half and the 128-key chunk (the
+    two softmax warps of a row each own one half), empty batches (exact 0),
+    and ragged query tiles (Lq = 130)."""
+    out, ref = _varlen_attention(lens, H=2, Lq=130, scale=0.125, seed=len(lens) + lens[0])
+    assert torch.isfinite(out).all()
+    for b, n in enumerate(lens):
+        if n == 0:
+            assert torch.equal(out[b], torch.zeros_like(out[b]))
+    torch.testing.assert_close(out, ref, rtol=2e-2, atol=2e-2)
+    _status_ok()
+
+
+def test_attention_rescales_each_half():
+    """Scores whose maximum keeps rising across chunks (each half re-bases its
+    running max and rescales its own accumulator), and a sharp softmax."""
+    out, ref = _varlen_attention([1500, 700, 64, 65], H=4, Lq=256, scale=0.125, seed=9,
+                                 key_growth=4.0, q_gain=3.0)
+    assert torch.isfinite(out).all()
+    torch.testing.assert_close(out, ref, rtol=2e-2, atol=3e-2)
+    _status_ok()
 
 
 def test_attention_temporal_mask():
