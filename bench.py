@@ -412,7 +412,7 @@ def kernel_class(name: str) -> str:
         return {0: "gemm_store", 1: "gemm_gelu", 2: "gemm_resid", 3: "gemm_bias"}[epi]
     if name.startswith("attn_"):
         return "attention"
-    if name.startswith("tokenize_kernel"):
+    if name.startswith("tokenize_kernel") or name.startswith("tok_fixup_kernel"):
         return "tokenizer"
     if name.startswith("pack_"):
         return "pack"
@@ -440,6 +440,8 @@ def forward_work(wl, B: int, E: int, idx_bytes: int, launches: dict) -> dict:
     vocab = c.max_neurons + c.max_time_bins + c.spike_value_buckets
     tok = 3 * E * idx_bytes + vocab * Din * es + E * Din * es
     pack = E * idx_bytes + E * 4
+    if "pack" not in launches:  # packed inside the tokenizer: batch indices and offsets
+        tok += E * idx_bytes + (B + 1) * 4
     head = BL * D * es
     n_norm = launches.get("norm", 0)
     norm = (2 * L * D * es + max(n_norm - 1, 0) * 2 * BL * D * es) if n_norm else 0
@@ -458,7 +460,8 @@ CLASS_DESC = {
     "gemm_gelu": "MLP up-projection GEMMs with the GELU epilogue",
     "gemm_store": "store GEMMs (q_proj, kv_proj, qkv_proj)",
     "attention": "cross- and self-attention (tcgen05, online softmax)",
-    "tokenizer": "spike tokenizer gather-sum + norm_kv",
+    "tokenizer": "spike tokenizer gather-sum + norm_kv (with the packing of sorted batch "
+                 "indices and the repack check launch, up to 2^20 events and 4096 windows)",
     "pack": "event packing (counts, offsets, dest)",
     "head": "behaviour head (head_prep + fused head)",
     "norm": "separate LayerNorm launches",

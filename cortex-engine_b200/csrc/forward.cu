@@ -1,8 +1,10 @@
 // Whole-forward driver: CortexModel.forward (cortex/models/cortex.py:90-122),
 // return_aux=False, launched as one stream of kernels with no host sync.
 //
-//   pack            counts/offsets/dest of the flat events     (_pack_events, :125-165)
-//   tokenize+LN_kv  gather-sum straight into packed order, norm_kv fused
+//   pack+tokenize   window offsets and the gather-sum straight into packed order,
+//                   norm_kv fused (_pack_events, :125-165): sorted batch indices
+//                   are packed inside the tokenizer; a second launch repacks
+//                   unsorted ones (stable counting sort) and tokenizes again
 //   LN_q, q_proj    batch-invariant latent queries, computed once per forward
 //   kv_proj         packed (E, 2D) keys|values                 (perceiver.py:67-69)
 //   cross attention varlen keys per sample, no padding          (perceiver.py:71-80)
@@ -36,7 +38,7 @@ constexpr float kLnEps = 1e-5f;
 size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t counts, offsets, dest, emax, packws, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
+  size_t counts, offsets, dest, emax, packws, tokslots, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
       qall, total;
 };
 
@@ -63,6 +65,7 @@ Layout plan(const ck_model* m, int64_t E, int32_t B) {
   o.dest = take((size_t)(E > 0 ? E : 1) * 4);
   o.emax = take(4);
   o.packws = take(pack_workspace_bytes(E, B));
+  o.tokslots = take(tokenize_packed_slots() * 4);
   o.xkv = take((size_t)(E > 0 ? E : 1) * Dh_in * es);
   o.kv = take((size_t)(E > 0 ? E : 1) * 2 * D * es);
   o.xq = take(L * D * es);
@@ -271,13 +274,23 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
   }
 
   if (io.stage != kFromKv) {
-    // 1. packing
-    CK_TRY(pack_events(bidx, idx_dt, 1, E, B, n_valid, counts, offsets, dest, emax,
-                       P(lay.packws), pack_workspace_bytes(E, B), st));
-    // 2. tokenizer + norm_kv, written in packed order
-    CK_TRY(tokenize(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din, m->n_vocab,
-                    m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1, 1, 1, E, dest,
-                    m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st, n_valid));
+    if (E > 0 && E <= kTokPackMaxE && B <= kTokPackMaxB) {
+      // 1+2. packing inside the tokenizer (+ norm_kv): sorted batch indices
+      // need no separate packing launches; a second launch repacks otherwise
+      CK_TRY(tokenize_packed(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din,
+                             m->n_vocab, m->t_vocab, m->v_vocab, nid, tb, val, bidx, idx_dt, E, B,
+                             m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, offsets,
+                             reinterpret_cast<int32_t*>(P(lay.tokslots)), st, n_valid));
+    } else {
+      // 1. packing
+      CK_TRY(pack_events(bidx, idx_dt, 1, E, B, n_valid, counts, offsets, dest, emax,
+                         P(lay.packws), pack_workspace_bytes(E, B), st));
+      // 2. tokenizer + norm_kv, written in packed order
+      CK_TRY(tokenize(m->neuron_emb, m->time_emb, m->value_emb, m->dtype, (int32_t)Din,
+                      m->n_vocab, m->t_vocab, m->v_vocab, Din, Din, Din, nid, tb, val, idx_dt, 1,
+                      1, 1, E, dest, m->norm_kv_w, m->norm_kv_b, kLnEps, P(lay.xkv), Din, st,
+                      n_valid));
+    }
   }
   // 4. packed keys|values
   if (io.stage != kFromKv && E > 0)

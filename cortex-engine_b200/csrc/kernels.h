@@ -147,6 +147,24 @@ int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
              const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
              cudaStream_t st, const int32_t* n_valid = nullptr);
 
+// Packing inside the tokenizer for the forward (tokenizer.cu): tokens of event
+// e go to row e and the window offsets come from the batch boundaries, which
+// is _pack_events' result when batch_indices is sorted (collate_events'
+// layout). A second launch checks the tokenizer blocks' flags (slots, at least
+// tokenize_packed_slots() words) and, for unsorted or out-of-range batch
+// indices, redoes the packing as a stable counting sort and tokenizes every
+// event into its packed row. dest is not produced. E <= kTokPackMaxE and
+// B <= kTokPackMaxB; larger batches use pack_events + tokenize.
+constexpr int64_t kTokPackMaxE = int64_t(1) << 20;
+constexpr int32_t kTokPackMaxB = 4096;
+size_t tokenize_packed_slots();
+int tokenize_packed(const void* n_emb, const void* t_emb, const void* v_emb, int dtype, int32_t D,
+                    int64_t n_vocab, int64_t t_vocab, int64_t v_vocab, const void* nid,
+                    const void* tb, const void* val, const void* bidx, int idx_dtype, int64_t E,
+                    int32_t B, const void* gamma, const void* beta, float eps, void* out,
+                    int64_t out_ld, int32_t* offsets, int32_t* slots, cudaStream_t st,
+                    const int32_t* n_valid);
+
 // event ingest from bin-count matrices (ingest.cu)
 size_t collate_bins_workspace_bytes(int32_t B, int32_t W);
 int collate_bins(const ck_bin_window* wins, int32_t B, int32_t W, int32_t n_buckets,

@@ -76,35 +76,41 @@ struct TokArgs {
   int64_t out_ld;
   int D;
   const int32_t* n_valid;
+  // Packing inside the tokenizer (tokenize_packed): the batch index of every
+  // event. Tokens go to row e (the packed row of sorted input), the window
+  // offsets come from the batch boundaries, and slots[block] records whether
+  // the block saw an event out of batch order or out of [0, B).
+  const void* bidx;
+  int64_t s_bidx;
+  int32_t B;
+  int32_t* offsets;
+  int32_t* slots;
 };
 
 // G lanes share one event row (G in {8, 16, 32}, so a warp handles 32 / G
 // events at once); each lane holds MAXV vectors of VEC elements. Index loads,
 // the three table gathers and the output store of the 32 / G rows are all
 // independent, so a warp keeps 3 * MAXV * (32 / G) 16-byte loads in flight.
+// One event row for the G lanes of a group: the three table rows summed, the
+// optional LayerNorm, the store to row dst_row (all 32 lanes of the warp call
+// it together: the row reductions shuffle across the whole warp).
+// tokenize_packed limits: the fix-up kernel keeps two B-sized histograms and
+// the destinations of E / kFixupCtas events in shared memory.
+constexpr int64_t kFixupCtas = 128;
+constexpr int kFixupMaxSmem =
+    (int)((2 * kTokPackMaxB + (kTokPackMaxE + kFixupCtas - 1) / kFixupCtas) * 4);
+
 template <typename T, int VEC, int MAXV, bool LN, int G>
-__global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const TokArgs a) {
-  grid_dep_wait();
-  grid_dep_launch();
-  constexpr int RPW = 32 / G;
+__device__ __forceinline__ void tok_event(const TokArgs& a, int64_t e, int64_t dst_row, bool live,
+                                          bool real, int sub) {
   constexpr bool kPair = std::is_same<T, __nv_bfloat16>::value && VEC == 8;
-  const int lane = threadIdx.x & 31;
-  const int sub = lane % G;
-  const int slot = lane / G;
-  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const T* ne = reinterpret_cast<const T*>(a.n_emb);
   const T* te = reinterpret_cast<const T*>(a.t_emb);
   const T* ve = reinterpret_cast<const T*>(a.v_emb);
   T* out = reinterpret_cast<T*>(a.out);
   const int nvec = a.D / VEC;
-  const int64_t nv = a.n_valid ? min((int64_t)max(*a.n_valid, 0), a.E) : a.E;
-  for (int64_t base = warp * RPW; base < a.E; base += nwarps * RPW) {
-    const int64_t e = base + slot;
-    const bool live = e < a.E;
-    const bool real = e < nv;
-    int64_t dst_row = -1, n = 0, t = 0, v = 0;
-    if (live) dst_row = a.dest ? (int64_t)a.dest[e] : e;
+  {
+    int64_t n = 0, t = 0, v = 0;
     if (real) {
       n = load_idx(a.nid, a.idx_dt, e, a.s_nid);
       t = load_idx(a.tb, a.idx_dt, e, a.s_tb);
@@ -253,13 +259,170 @@ __global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const 
 }
 
 template <typename T, int VEC, int MAXV, bool LN, int G>
+__global__ void __launch_bounds__(256, MAXV <= 4 ? 3 : 1) tokenize_kernel(const TokArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  constexpr int RPW = 32 / G;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % G;
+  const int slot = lane / G;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t nv = a.n_valid ? min((int64_t)max(*a.n_valid, 0), a.E) : a.E;
+  int viol = 0;
+  if (a.bidx != nullptr && nv == 0 && blockIdx.x == 0)
+    for (int64_t bb = threadIdx.x; bb <= a.B; bb += blockDim.x) a.offsets[bb] = 0;
+  for (int64_t base = warp * RPW; base < a.E; base += nwarps * RPW) {
+    const int64_t e = base + slot;
+    const bool live = e < a.E;
+    const bool real = e < nv;
+    int64_t dst_row = -1;
+    if (live) dst_row = a.dest ? (int64_t)a.dest[e] : e;
+    if (a.bidx != nullptr && real && sub == 0) {
+      // sorted input: the window offsets are the batch boundaries
+      const int64_t b = load_idx(a.bidx, a.idx_dt, e, a.s_bidx);
+      const int64_t bp = e > 0 ? load_idx(a.bidx, a.idx_dt, e - 1, a.s_bidx) : -1;
+      if (b < 0 || b >= a.B || bp > b) {
+        viol = 1;
+      } else {
+        for (int64_t bb = max(bp + 1, (int64_t)0); bb <= b; ++bb) a.offsets[bb] = (int32_t)e;
+        if (e == nv - 1)
+          for (int64_t bb = b + 1; bb <= a.B; ++bb) a.offsets[bb] = (int32_t)nv;
+      }
+    }
+    tok_event<T, VEC, MAXV, LN, G>(a, e, dst_row, live, real, sub);
+  }
+  if (a.slots != nullptr) {
+    const int any = __syncthreads_or(viol);
+    if (threadIdx.x == 0) a.slots[blockIdx.x] = any;
+  }
+}
+
+// Exclusive scan of v[0..n) in place by one CTA of 256 threads (each a
+// contiguous run); returns the total to every thread.
+__device__ int32_t block_scan_runs(int32_t* v, int64_t n) {
+  __shared__ int32_t wtot[8];
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int64_t per = (n + 255) / 256;
+  const int64_t lo = min(n, t * per), hi = min(n, lo + per);
+  int32_t sum = 0;
+  for (int64_t i = lo; i < hi; ++i) sum += v[i];
+  int32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) wtot[w] = incl;
+  __syncthreads();
+  int32_t before = 0, total = 0;
+  for (int k = 0; k < 8; ++k) {
+    if (k < w) before += wtot[k];
+    total += wtot[k];
+  }
+  int32_t run = before + incl - sum;
+  for (int64_t i = lo; i < hi; ++i) {
+    const int32_t c = v[i];
+    v[i] = run;
+    run += c;
+  }
+  __syncthreads();
+  return total;
+}
+
+// The general packing for tokenize_packed, one launch after the tokenizer:
+// nothing to do unless a tokenizer block saw an event out of batch order or
+// out of [0, B). Otherwise every CTA counts the events of each window over
+// the whole batch and before its own segment of `chunk` events (dynamic
+// shared memory: two B-sized histograms and the segment's destinations),
+// rebuilds the window offsets (CTA 0 stores them), gives each event of its
+// segment its packed row (offset + rank among earlier events of its window,
+// the stable order of _pack_events) and tokenizes it into that row again.
+template <typename T, int VEC, int MAXV, bool LN, int G>
+__global__ void __launch_bounds__(256) tok_fixup_kernel(const TokArgs a, const int32_t n_slots,
+                                                        const int64_t chunk) {
+  grid_dep_wait();
+  grid_dep_launch();
+  int viol = 0;
+  for (int i = threadIdx.x; i < n_slots; i += blockDim.x) viol |= a.slots[i];
+  if (!__syncthreads_or(viol)) return;
+  extern __shared__ int32_t fx[];
+  int32_t* hist = fx;           // [B] events per window, then the window offsets
+  int32_t* cur = fx + a.B;      // [B] events before this segment, then the row cursor
+  int32_t* dst = fx + 2 * a.B;  // [chunk] packed rows of the segment's events
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t nv = a.n_valid ? min((int64_t)max(*a.n_valid, 0), a.E) : a.E;
+  const int64_t s0 = blockIdx.x * chunk, s1 = min(s0 + chunk, a.E);
+  for (int64_t i = tid; i < a.B; i += blockDim.x) hist[i] = cur[i] = 0;
+  __syncthreads();
+  for (int64_t e = tid; e < nv; e += blockDim.x) {
+    const int64_t b = load_idx(a.bidx, a.idx_dt, e, a.s_bidx);
+    if (b >= 0 && b < a.B) {
+      atomicAdd(&hist[b], 1);
+      if (e < s0) atomicAdd(&cur[b], 1);
+    }
+  }
+  __syncthreads();
+  const int32_t total = block_scan_runs(hist, a.B);
+  if (blockIdx.x == 0) {
+    for (int64_t i = tid; i < a.B; i += blockDim.x) a.offsets[i] = hist[i];
+    if (tid == 0) a.offsets[a.B] = total;
+  }
+  for (int64_t i = tid; i < a.B; i += blockDim.x) cur[i] += hist[i];
+  __syncthreads();
+  if (wid == 0) {  // in event order, 32 at a time
+    for (int64_t base = s0; base < s1; base += 32) {
+      const int64_t e = base + lane;
+      const bool in = e < s1;
+      int64_t b = -1;  // padding or past the segment
+      if (in && e < nv) {
+        b = load_idx(a.bidx, a.idx_dt, e, a.s_bidx);
+        if (b < 0 || b >= a.B) {
+          set_status(CK_ERR_INDEX, (int)e, (int)b);
+          b = -2;  // dropped, as _pack_events' index check would reject it
+        }
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, (long long)b);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      int32_t d = (in && e >= nv) ? (int32_t)e : -1;  // padding keeps its own (zero) row
+      if (b >= 0) d = cur[b] + rank;
+      __syncwarp();
+      if (b >= 0 && rank == 0) cur[b] += __popc(peers);
+      __syncwarp();
+      if (in) dst[e - s0] = d;
+    }
+  }
+  __syncthreads();
+  constexpr int RPW = 32 / G;
+  const int sub = lane % G, slot = lane / G;
+  for (int64_t base = s0 + wid * RPW; base < s1; base += (blockDim.x / 32) * RPW) {
+    const int64_t e = base + slot;
+    const bool live = e < s1;
+    tok_event<T, VEC, MAXV, LN, G>(a, e, live ? (int64_t)dst[e - s0] : -1, live, live && e < nv,
+                                   sub);
+  }
+}
+
+template <typename T, int VEC, int MAXV, bool LN, int G>
 int launch_tok(const TokArgs& a, cudaStream_t st) {
   constexpr int rows_per_block = 8 * (32 / G);
   int64_t blocks = (a.E + rows_per_block - 1) / rows_per_block;
   const int64_t cap = 16 * (int64_t)num_sms();
   if (blocks > cap) blocks = cap;
-  return launch_pdl(tokenize_kernel<T, VEC, MAXV, LN, G>, dim3((unsigned)blocks), dim3(256), 0,
-                    st, a);
+  const int rc = launch_pdl(tokenize_kernel<T, VEC, MAXV, LN, G>, dim3((unsigned)blocks),
+                            dim3(256), 0, st, a);
+  if (rc != CK_OK || a.bidx == nullptr) return rc;
+  // the general packing, for input that turns out not to be sorted
+  int64_t chunk = (a.E + kFixupCtas - 1) / kFixupCtas;
+  if (chunk < 1024) chunk = 1024;
+  chunk = (chunk + 31) & ~int64_t(31);
+  const int64_t fblocks = (a.E + chunk - 1) / chunk;
+  const size_t smem = (size_t)(2 * (int64_t)a.B + chunk) * 4;
+  auto fk = tok_fixup_kernel<T, VEC, MAXV, LN, G>;
+  if (smem > (size_t)kFixupMaxSmem) return CK_ERR_INVALID_ARG;
+  if (!smem_attr_ready(reinterpret_cast<const void*>(fk), kFixupMaxSmem))
+    return record_cuda_error();
+  return launch_pdl(fk, dim3((unsigned)fblocks), dim3(256), smem, st, a, (int32_t)blocks, chunk);
 }
 
 template <typename T, int VEC, int MAXV, int G>
@@ -303,6 +466,32 @@ int tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
   const bool vec_ok = ((int64_t)D * es) % 16 == 0 && (n_ld * es) % 16 == 0 &&
                       (t_ld * es) % 16 == 0 && (v_ld * es) % 16 == 0 && (out_ld * es) % 16 == 0 &&
                       al16(n_emb) && al16(t_emb) && al16(v_emb) && al16(out) &&
+                      (gamma == nullptr || al16(gamma)) && (beta == nullptr || al16(beta));
+  if (dtype == CK_BF16) return dispatch_tok<__nv_bfloat16>(a, vec_ok, st);
+  if (dtype == CK_F32) return dispatch_tok<float>(a, vec_ok, st);
+  return CK_ERR_UNSUPPORTED;
+}
+
+size_t tokenize_packed_slots() { return (size_t)16 * num_sms(); }
+
+int tokenize_packed(const void* n_emb, const void* t_emb, const void* v_emb, int dtype, int32_t D,
+                    int64_t n_vocab, int64_t t_vocab, int64_t v_vocab, const void* nid,
+                    const void* tb, const void* val, const void* bidx, int idx_dtype, int64_t E,
+                    int32_t B, const void* gamma, const void* beta, float eps, void* out,
+                    int64_t out_ld, int32_t* offsets, int32_t* slots, cudaStream_t st,
+                    const int32_t* n_valid) {
+  if (E <= 0 || E > kTokPackMaxE || B <= 0 || B > kTokPackMaxB || bidx == nullptr ||
+      offsets == nullptr || slots == nullptr)
+    return CK_ERR_INVALID_ARG;
+  if (idx_dtype != CK_I64 && idx_dtype != CK_I32) return CK_ERR_UNSUPPORTED;
+  if (!n_emb || !t_emb || !v_emb || !nid || !tb || !val || !out) return CK_ERR_INVALID_ARG;
+  TokArgs a{n_emb, t_emb, v_emb, n_vocab, t_vocab, v_vocab, D, D, D, nid, tb, val, idx_dtype,
+            1, 1, 1, E, nullptr, gamma, beta, eps, out, out_ld, D, n_valid,
+            bidx, 1, B, offsets, slots};
+  const int es = dtype == CK_F32 ? 4 : 2;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec_ok = ((int64_t)D * es) % 16 == 0 && (out_ld * es) % 16 == 0 && al16(n_emb) &&
+                      al16(t_emb) && al16(v_emb) && al16(out) &&
                       (gamma == nullptr || al16(gamma)) && (beta == nullptr || al16(beta));
   if (dtype == CK_BF16) return dispatch_tok<__nv_bfloat16>(a, vec_ok, st);
   if (dtype == CK_F32) return dispatch_tok<float>(a, vec_ok, st);

@@ -179,6 +179,50 @@ def test_interleaved_events_and_int32_indices():
     assert torch.equal(as32, base)
 
 
+def test_unsorted_device_indices_repack_bit_identical():
+    """Batch indices in random order (device tensors): the tokenizer's own
+    packing sees them out of order and the repacking launch redoes it as a
+    stable counting sort. The result equals the forward over the same events
+    stably sorted by window (the packed rows are the same), including an empty
+    window and windows after the last event."""
+    from cortex import _lib
+
+    wl, model = _model("cfg1")
+    g = torch.Generator().manual_seed(5)
+    counts = [37, 0, 300, 1, 129, 64, 700, 5]
+    E = sum(counts)
+    bidx = torch.cat([torch.full((c,), w) for w, c in enumerate(counts)]).long()
+    nid = torch.randint(0, 137, (E,), generator=g)
+    tb = torch.randint(0, 600, (E,), generator=g)
+    val = torch.randint(0, 8, (E,), generator=g)
+    perm = torch.randperm(E, generator=g)
+    ev = [t[perm].to(DEV) for t in (nid, tb, val, bidx)]
+    order = torch.sort(bidx[perm], stable=True).indices
+    srt = [t[order] for t in ev]
+    with torch.no_grad():
+        y = model(*ev, batch_size=10)["behavior"]
+        ys = model(*srt, batch_size=10)["behavior"]
+    assert torch.equal(y, ys)
+    assert torch.equal(y[1], y[8]) and torch.equal(y[8], y[9])  # no events
+    assert _lib.device_status()[0] == 0
+
+
+def test_out_of_range_device_batch_index_sets_status():
+    from cortex import _lib
+
+    wl, model = _model("cfg1")
+    nid = torch.tensor([1, 2, 3, 4], device=DEV)
+    tb = torch.tensor([1, 2, 3, 4], device=DEV)
+    val = torch.tensor([1, 2, 3, 4], device=DEV)
+    with torch.no_grad():
+        model(nid, tb, val, torch.tensor([0, 0, 1, 1], device=DEV), batch_size=2)
+        torch.cuda.synchronize()
+        assert _lib.device_status()[0] == 0
+        model(nid, tb, val, torch.tensor([0, 5, 1, 1], device=DEV), batch_size=2)
+        torch.cuda.synchronize()
+    assert _lib.device_status()[0] == _lib.CK_ERR_INDEX
+
+
 def test_module_path_matches_fused_path():
     """return_aux=True runs the composed module forwards (padded tokens + mask)."""
     from cortex.workloads import make_inputs
