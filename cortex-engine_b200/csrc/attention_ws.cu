@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;    // [STAGES]
   uint64_t* v_full = bars + 4;    // [STAGES]
-  uint64_t* kv_empty = bars + 6;  // [STAGES]
+  uint64_t* k_empty = bars + 6;   // [STAGES] the stage's K was read by its QK^T
   uint64_t* s_full = bars + 8;
   uint64_t* s_free = bars + 9;
   uint64_t* p_full = bars + 10;   // [2 key halves]
@@ -174,7 +174,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
   uint64_t* o_free = bars + 14;
   uint64_t* drain = bars + 15;
   uint64_t* x_ready = bars + 16;  // [4 lane quarters]: half 1 published c_1, O_1 / l_1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* v_empty = bars + 20;  // [STAGES] the stage's V was read by its two P V products
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x;
@@ -187,7 +188,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, NSOFT);
@@ -230,13 +232,19 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
         ++nq;
         for (int j = 0; j < it.nch; ++j, ++g) {
           const int st = g & 1;
-          if (!mbar_wait(&kv_empty[st], (uint32_t)(((g >> 1) & 1) ^ 1), abort_flag, 41)) {
+          // K and V of a stage are released separately: the next K can load
+          // as soon as the QK^T that read this one is done
+          uint8_t* kv = sKV + st * 2 * KV_BYTES;
+          if (!mbar_wait(&k_empty[st], (uint32_t)(((g >> 1) & 1) ^ 1), abort_flag, 41)) {
             ok = false;
             break;
           }
-          uint8_t* kv = sKV + st * 2 * KV_BYTES;
           mbar_arrive_expect_tx(&k_full[st], KV_BYTES);
           tma_load_2d(kv, &tmK, &k_full[st], it.k_col, it.k_row + j * KC);
+          if (!mbar_wait(&v_empty[st], (uint32_t)(((g >> 1) & 1) ^ 1), abort_flag, 41)) {
+            ok = false;
+            break;
+          }
           mbar_arrive_expect_tx(&v_full[st], KV_BYTES);
           tma_load_2d(kv + KV_BYTES, &tmV, &v_full[st], it.v_col, it.v_row + j * KC);
           ++kv_loads[st];
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
           }
           tc_commit(&o_full[h]);
         }
-        tc_commit(&kv_empty[st]);
+        tc_commit(&v_empty[st]);
         return true;
       };
       for (int w = blockIdx.x; w < p.num_items && ok; w += gridDim.x) {
@@ -298,6 +306,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
             tc_mma_ss(tmem_s, sw128_desc(qa + k * 32, 16, 1024),
                       sw128_desc(ka + k * 32, 16, 1024), IDESC_S, k != 0);
           tc_commit(s_full);
+          tc_commit(&k_empty[st]);
           if (j == it.nch - 1) tc_commit(q_empty);
           if (pv_g >= 0 && !issue_pv()) {
             ok = false;
