@@ -82,6 +82,28 @@ def tokenize(n_emb, t_emb, v_emb, nid, tb, val, dest=None, gamma=None, beta=None
     return out
 
 
+def tokenize_packed(n_emb, t_emb, v_emb, nid, tb, val, batch_indices, batch_size: int,
+                    gamma=None, beta=None, eps: float = 1e-5):
+    """Window offsets and tokens in packed order in one call (ck_tokenize_packed):
+    (tokens (E, D), offsets (B + 1,) int32). Tables and index arrays contiguous."""
+    dev = L.require_cuda(n_emb, t_emb, v_emb, nid, tb, val, batch_indices, what="tokenize_packed")
+    lib = L.load()
+    E, D = nid.shape[0], n_emb.shape[1]
+    idx = [t.to(nid.dtype).contiguous() for t in (nid, tb, val, batch_indices)]
+    tabs = [t.contiguous() for t in (n_emb, t_emb, v_emb)]
+    out = torch.empty(max(E, 1), D, dtype=n_emb.dtype, device=dev)
+    offsets = torch.empty(batch_size + 1, dtype=torch.int32, device=dev)
+    ws_bytes = lib.ck_tokenize_packed_workspace_bytes()
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    rc = lib.ck_tokenize_packed(
+        L.ptr(tabs[0]), L.ptr(tabs[1]), L.ptr(tabs[2]), L.dtype_code(n_emb.dtype), D,
+        n_emb.shape[0], t_emb.shape[0], v_emb.shape[0], *(L.ptr(t) for t in idx),
+        _idx_code(idx[0]), E, batch_size, L.ptr(gamma), L.ptr(beta), eps, L.ptr(out), D,
+        L.ptr(offsets), L.ptr(ws), ws_bytes, L.stream_of(dev))
+    L.check(rc, "ck_tokenize_packed")
+    return out[:E], offsets
+
+
 def row_norm(x: torch.Tensor, gamma, beta, eps: float, mode: int = L.CK_NORM_LAYER, out=None):
     dev = L.require_cuda(x, gamma, what="row_norm")
     D = x.shape[-1]

@@ -131,6 +131,27 @@ int ck_tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dty
                   S(stream));
 }
 
+size_t ck_tokenize_packed_workspace_bytes(void) { return tokenize_packed_slots() * 4; }
+
+int ck_tokenize_packed(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
+                       int32_t D, int64_t n_vocab, int64_t t_vocab, int64_t v_vocab,
+                       const void* nid, const void* tb, const void* val, const void* batch_indices,
+                       int idx_dtype, int64_t E, int32_t B, const void* gamma, const void* beta,
+                       float eps, void* out, int64_t out_ld, int32_t* offsets, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (E < 0 || B <= 0 || offsets == nullptr) return CK_ERR_INVALID_ARG;
+  if (E > kTokPackMaxE || B > kTokPackMaxB) return CK_ERR_UNSUPPORTED;
+  if (E == 0)  // no events: every window is empty
+    return cudaMemsetAsync(offsets, 0, (size_t)(B + 1) * 4, S(stream)) == cudaSuccess
+               ? CK_OK
+               : record_cuda_error();
+  if (workspace == nullptr || workspace_bytes < tokenize_packed_slots() * 4)
+    return CK_ERR_WORKSPACE;
+  return tokenize_packed(n_emb, t_emb, v_emb, dtype, D, n_vocab, t_vocab, v_vocab, nid, tb, val,
+                         batch_indices, idx_dtype, E, B, gamma, beta, eps, out, out_ld, offsets,
+                         reinterpret_cast<int32_t*>(workspace), S(stream), nullptr);
+}
+
 int ck_row_norm(const void* x, int dtype, int64_t M, int32_t D, int64_t ldx, const void* gamma,
                 const void* beta, float eps, int mode, void* y, int64_t ldy, void* stream) {
   return row_norm(x, dtype, M, D, ldx, gamma, beta, eps, mode, y, ldy, S(stream));

@@ -112,6 +112,27 @@ int ck_tokenize(const void* n_emb, const void* t_emb, const void* v_emb, int dty
                 const void* gamma, const void* beta, float eps, void* out, int64_t out_ld,
                 void* stream);
 
+/* Packing fused into the tokenizer: _pack_events' window offsets
+ * (cortex/models/cortex.py:125-165) and the tokens in packed order in one
+ * call, for contiguous tables (row stride D) and index arrays. Sorted
+ * batch_indices (collate_events' layout) are packed inside the tokenizer
+ * launch: tokens of event e go to row e, offsets[b] is the first event of
+ * window b. A second launch checks the tokenizer blocks' flags and, when an
+ * index is out of order or outside [0, B), redoes the packing as a stable
+ * counting sort and tokenizes every event into its packed row (out-of-range
+ * events are dropped with CK_ERR_INDEX in the status word, as ck_pack_events
+ * does). offsets has B + 1 entries. workspace: at least
+ * ck_tokenize_packed_workspace_bytes() bytes, contents arbitrary. Batches of
+ * more than 2^20 events or 4096 windows return CK_ERR_UNSUPPORTED (use
+ * ck_pack_events + ck_tokenize). */
+size_t ck_tokenize_packed_workspace_bytes(void);
+int ck_tokenize_packed(const void* n_emb, const void* t_emb, const void* v_emb, int dtype,
+                       int32_t D, int64_t n_vocab, int64_t t_vocab, int64_t v_vocab,
+                       const void* nid, const void* tb, const void* val, const void* batch_indices,
+                       int idx_dtype, int64_t E, int32_t B, const void* gamma, const void* beta,
+                       float eps, void* out, int64_t out_ld, int32_t* offsets, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* ── 3. row norm ────────────────────────────────────────────────────────────
  * nn.LayerNorm (cortex/models/perceiver.py:51-52,97-98,143) or the RMSNorm of
  * rms_norm_linear_reference (cortex/kernels/fused_rmsnorm.py:86-108), fp32

@@ -169,6 +169,56 @@ def test_tokenizer_with_fused_layernorm():
     assert _lib.device_status()[0] == 0
 
 
+@pytest.mark.parametrize("order", ["sorted", "shuffled"])
+@pytest.mark.parametrize("dtype,ln,idx", [(torch.bfloat16, True, torch.int64),
+                                          (torch.bfloat16, False, torch.int32),
+                                          (torch.float32, True, torch.int64)])
+def test_tokenize_packed_matches_pack_then_tokenize(order, dtype, ln, idx):
+    """ck_tokenize_packed (packing inside the tokenizer, with the repack launch
+    for unsorted input) against ck_pack_events + ck_tokenize: the same offsets
+    and bit-identical tokens in every packed row, with empty windows at the
+    start, inside and at the end."""
+    from cortex import _lib
+    from cortex.kernels import _ops
+
+    counts = [0, 37, 0, 300, 1, 129, 64, 700, 5, 0, 0]
+    B, E = len(counts), sum(counts)
+    bidx = torch.cat([torch.full((c,), w) for w, c in enumerate(counts)]).to(idx)
+    n, t, v = _embs(512, 1024, 8, 512, dtype)
+    nid, tb, val = (x.to(idx) for x in _ids(E, 512, 1024, 8))
+    if order == "shuffled":
+        perm = torch.randperm(E, generator=torch.Generator().manual_seed(3))
+        nid, tb, val, bidx = nid[perm], tb[perm], val[perm], bidx[perm]
+    g = (torch.rand(512) + 0.5).to(dtype) if ln else None
+    b = (torch.randn(512) * 0.1).to(dtype) if ln else None
+    d = [x.to(DEV) for x in (n, t, v, nid, tb, val, bidx)]
+    gd = g.to(DEV) if ln else None
+    bd = b.to(DEV) if ln else None
+    tok, offs = _ops.tokenize_packed(*d, B, gamma=gd, beta=bd, eps=1e-5)
+    counts_ref, offs_ref, dest, _ = _ops.pack_events(d[6], B)
+    ref = _ops.tokenize(*d[:6], dest=dest, gamma=gd, beta=bd, eps=1e-5, out_rows=E)
+    assert torch.equal(offs, offs_ref)
+    assert torch.equal(tok, ref)
+    assert _lib.device_status()[0] == 0
+
+
+def test_tokenize_packed_out_of_range_window_index():
+    """An index outside [0, B) is dropped with CK_ERR_INDEX, as ck_pack_events does."""
+    from cortex import _lib
+    from cortex.kernels import _ops
+
+    n, t, v = _embs(512, 1024, 8, 512, torch.bfloat16)
+    nid, tb, val = _ids(6, 512, 1024, 8)
+    bidx = torch.tensor([0, 0, 1, 7, 1, 2])
+    d = [x.to(DEV) for x in (n, t, v, nid, tb, val, bidx)]
+    tok, offs = _ops.tokenize_packed(*d, 3)
+    torch.cuda.synchronize()
+    assert _lib.device_status()[0] == _lib.CK_ERR_INDEX
+    assert offs.cpu().tolist() == [0, 2, 4, 5]
+    ref = _ops.tokenize(*d[:6])
+    assert torch.equal(tok[:5], ref[[0, 1, 2, 4, 5]])
+
+
 # ── row norm ─────────────────────────────────────────────────────────────────
 
 
