@@ -162,6 +162,30 @@ def test_windows_are_independent(name):
             assert torch.equal(y[0], full[b]), b
 
 
+@pytest.mark.parametrize("name,batch", [("cfg3", 64), ("cfg4", 12)])
+def test_sharded_decode_is_the_full_batch_decode(name, batch):
+    """The N > 1 path of bench.py and of a multi-GPU deployment, on the product:
+    the batch split by shard_bounds (ranges balanced by events) and
+    slice_events (batch indices rebased), each shard decoded on its own, gives
+    bit-for-bit the full-batch decode for 2, 3 and 8 shards."""
+    from cortex.sharding import shard_bounds, slice_events
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    inp, counts = make_inputs(wl, seed=11, batch=batch)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    ev = {k: v.numpy() for k, v in inp.items()}
+    with torch.no_grad():
+        full = model(*(inp[k].to(DEV) for k in cols))["behavior"]
+        for world in (2, 3, 8):
+            parts = []
+            for b0, b1 in shard_bounds(counts, world):
+                one = slice_events(ev, counts, b0, b1)
+                parts.append(model(*(torch.from_numpy(one[k]).to(DEV) for k in cols),
+                                   batch_size=b1 - b0)["behavior"])
+            assert torch.equal(torch.cat(parts), full), world
+
+
 def test_interleaved_events_and_int32_indices():
     from cortex.workloads import make_inputs
 
