@@ -416,6 +416,8 @@ def kernel_class(name: str) -> str:
         return "attention"
     if name.startswith("tokenize_kernel") or name.startswith("tok_fixup_kernel"):
         return "tokenizer"
+    if name.startswith("dequant_kernel"):
+        return "dequant"
     if name.startswith("pack_"):
         return "pack"
     if name.startswith("head_"):
@@ -448,11 +450,14 @@ def forward_work(wl, B: int, E: int, idx_bytes: int, launches: dict) -> dict:
     n_norm = launches.get("norm", 0)
     norm = (2 * L * D * es + max(n_norm - 1, 0) * 2 * BL * D * es) if n_norm else 0
     int8 = layers * 2 * BL * (D * 3 * D + D * D + D * Hm + Hm * D) if wl.int8 else 0
+    # INT8 weights dequantised to bf16 once per forward: int8 read, bf16 written, scales
+    n8 = layers * (D * 3 * D + D * D + D * Hm + Hm * D) if wl.int8 else 0
+    deq = 3 * n8 + 4 * layers * (3 * D + D + Hm + D)
     return {
         "gemm_store": ("tensor", store), "gemm_gelu": ("tensor", gelu),
         "gemm_resid": ("tensor", resid), "attention": ("tensor", attn),
         "tokenizer": ("hbm", tok), "pack": ("hbm", pack), "head": ("hbm", head),
-        "norm": ("hbm", norm), "_int8_flops": int8,
+        "norm": ("hbm", norm), "dequant": ("hbm", deq), "_int8_flops": int8,
     }
 
 
@@ -467,6 +472,8 @@ CLASS_DESC = {
     "pack": "event packing (counts, offsets, dest)",
     "head": "behaviour head (head_prep + fused head)",
     "norm": "separate LayerNorm launches",
+    "dequant": "INT8 block weights dequantised to bf16 once per forward (QuantizedLinear's "
+               "expression; the GEMM classes then run on them)",
 }
 
 
@@ -535,7 +542,15 @@ def rooflines(wl, B, E, idx_bytes, per_kernel, name_for_traffic):
             e["traffic_note"] = tr["note"]
         out.append(e)
     int8 = None
-    if work["_int8_flops"]:
+    dq = next((e for e in out if e["class"] == "dequant"), None)
+    if work["_int8_flops"] and dq is not None:
+        int8 = {"what": "the INT8 linears (qkv, out_proj, mlp.0, mlp.2 of every block) run as "
+                        "bf16 GEMMs (counted in the GEMM classes) on weights dequantised once "
+                        "per forward by the dequant class",
+                "dequant_ms_per_forward": dq["ms_per_forward"],
+                "dequant_frac_of_hbm": dq.get("frac"),
+                "int8_linear_flops": int(work["_int8_flops"])}
+    elif work["_int8_flops"]:
         t8 = sum(ms for k, (n, ms) in per_kernel.items()
                  if _GEMM_RE.match(k) and _GEMM_RE.match(k).group(2) == "2")
         if t8 > 0:

@@ -28,6 +28,7 @@ SOURCES = [
     "status.cu",
     "pack.cu",
     "tokenizer.cu",
+    "dequant.cu",
     "norm.cu",
     "gemm_tc.cu",
     "gemm_simt.cu",

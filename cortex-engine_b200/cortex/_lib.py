@@ -109,6 +109,7 @@ _SIGS = {
     "ck_tokenize": (_int, [_vp, _vp, _vp, _int, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                            _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _f32, _vp,
                            _i64, _vp]),
+    "ck_dequantize_int8": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "ck_tokenize_packed_workspace_bytes": (_sz, []),
     "ck_tokenize_packed": (_int, [_vp, _vp, _vp, _int, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp,
                                   _int, _i64, _i32, _vp, _vp, _f32, _vp, _i64, _vp, _vp, _sz,

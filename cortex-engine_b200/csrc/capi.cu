@@ -152,6 +152,14 @@ int ck_tokenize_packed(const void* n_emb, const void* t_emb, const void* v_emb, 
                          reinterpret_cast<int32_t*>(workspace), S(stream), nullptr);
 }
 
+int ck_dequantize_int8(const void* w_int8, const float* scale, int64_t N, int64_t K, int64_t ldw,
+                       void* out, int64_t ldo, void* stream) {
+  if (N == 0) return CK_OK;
+  DequantSeg g{reinterpret_cast<const int8_t*>(w_int8), scale, out, N, K, ldw, ldo};
+  if (!dequant_seg_ok(g)) return CK_ERR_INVALID_ARG;
+  return dequant_int8(&g, 1, S(stream));
+}
+
 int ck_row_norm(const void* x, int dtype, int64_t M, int32_t D, int64_t ldx, const void* gamma,
                 const void* beta, float eps, int mode, void* y, int64_t ldy, void* stream) {
   return row_norm(x, dtype, M, D, ldx, gamma, beta, eps, mode, y, ldy, S(stream));

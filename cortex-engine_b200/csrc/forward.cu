@@ -18,6 +18,8 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <vector>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -38,7 +40,7 @@ constexpr float kLnEps = 1e-5f;
 size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t counts, offsets, dest, emax, packws, tokslots, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
+  size_t counts, offsets, dest, emax, packws, tokslots, wdeq, xkv, kv, xq, qc, lat, x, qkv, att, hbuf, qh, oh,
       qall, total;
 };
 
@@ -47,6 +49,44 @@ struct Layout {
 bool use_fused_head(const ck_model* m) {
   const char* v = std::getenv("CK_HEAD_FUSED");
   return (v == nullptr || std::strcmp(v, "0") != 0) && head_fused_supported(m);
+}
+
+// The INT8 linears of the self-attention blocks that the forward dequantises
+// to bf16 once per call (bf16 models; K a multiple of 16 and 16-byte aligned
+// weights), in block order qkv, out, mlp.0, mlp.2, with their (N, K).
+struct DeqPlan {
+  int n = 0;
+  size_t bytes = 0;
+};
+
+int64_t block_lin_n(const ck_model* m, int j) {
+  const int64_t D = m->latent_dim, Hm = m->mlp_hidden;
+  return j == 0 ? 3 * D : (j == 2 ? Hm : D);
+}
+int64_t block_lin_k(const ck_model* m, int j) {
+  return j == 3 ? (int64_t)m->mlp_hidden : (int64_t)m->latent_dim;
+}
+const ck_linear_weight& block_lin(const ck_block_weights& w, int j) {
+  return j == 0 ? w.qkv : (j == 1 ? w.out : (j == 2 ? w.mlp0 : w.mlp2));
+}
+bool dequantised(const ck_model* m, const ck_linear_weight& lw, int64_t N, int64_t K) {
+  if (m->dtype != CK_BF16 || lw.dtype != CK_I8 || lw.w == nullptr || lw.scale == nullptr)
+    return false;
+  DequantSeg g{reinterpret_cast<const int8_t*>(lw.w), lw.scale,
+               reinterpret_cast<void*>(uintptr_t(256)), N, K, K, K};
+  return dequant_seg_ok(g);
+}
+DeqPlan deq_plan(const ck_model* m) {
+  DeqPlan d;
+  for (int i = 0; i < m->num_layers && m->blocks != nullptr; ++i)
+    for (int j = 0; j < 4; ++j) {
+      const int64_t N = block_lin_n(m, j), K = block_lin_k(m, j);
+      if (dequantised(m, block_lin(m->blocks[i], j), N, K)) {
+        ++d.n;
+        d.bytes += (size_t)N * K * 2;
+      }
+    }
+  return d;
 }
 
 Layout plan(const ck_model* m, int64_t E, int32_t B) {
@@ -66,6 +106,7 @@ Layout plan(const ck_model* m, int64_t E, int32_t B) {
   o.emax = take(4);
   o.packws = take(pack_workspace_bytes(E, B));
   o.tokslots = take(tokenize_packed_slots() * 4);
+  o.wdeq = take(deq_plan(m).bytes + 256);
   o.xkv = take((size_t)(E > 0 ? E : 1) * Dh_in * es);
   o.kv = take((size_t)(E > 0 ? E : 1) * 2 * D * es);
   o.xq = take(L * D * es);
@@ -106,6 +147,7 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 struct SideStream {
   cudaStream_t s = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  cudaEvent_t deq = nullptr;  // the INT8 weights' dequantisation is done
 };
 
 // A host thread's side streams, released when the thread exits (errors are
@@ -118,6 +160,7 @@ struct SideStreams {
       if (ss.s) cudaStreamDestroy(ss.s);
       if (ss.fork) cudaEventDestroy(ss.fork);
       if (ss.join) cudaEventDestroy(ss.join);
+      if (ss.deq) cudaEventDestroy(ss.deq);
     }
   }
 };
@@ -135,11 +178,13 @@ SideStream* side_stream() {
     SideStream n;
     if (cudaStreamCreateWithFlags(&n.s, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess) {
+        cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&n.deq, cudaEventDisableTiming) != cudaSuccess) {
       (void)cudaGetLastError();
       if (n.s) cudaStreamDestroy(n.s);
       if (n.fork) cudaEventDestroy(n.fork);
       if (n.join) cudaEventDestroy(n.join);
+      if (n.deq) cudaEventDestroy(n.deq);
       return nullptr;
     }
     ss = n;
@@ -250,6 +295,29 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
   } while (0)
 
   cudaEvent_t join_ev = nullptr;  // the side stream's prologue is done
+  cudaEvent_t deq_ev = nullptr;   // the side stream's dequantisation is done
+
+  // The blocks' INT8 linears as bf16 weights in the workspace (dequantised
+  // below, once per forward), or the module's own weights.
+  std::vector<ck_linear_weight> bw((size_t)m->num_layers * 4);
+  std::vector<DequantSeg> deq;
+  {
+    uint8_t* wq = reinterpret_cast<uint8_t*>(P(lay.wdeq));
+    for (int i = 0; i < m->num_layers; ++i)
+      for (int j = 0; j < 4; ++j) {
+        const ck_linear_weight& lw = block_lin(m->blocks[i], j);
+        const int64_t N = block_lin_n(m, j), K = block_lin_k(m, j);
+        ck_linear_weight& o = bw[(size_t)i * 4 + j];
+        o = lw;
+        if (dequantised(m, lw, N, K)) {
+          deq.push_back(DequantSeg{reinterpret_cast<const int8_t*>(lw.w), lw.scale, wq, N, K, K, K});
+          o.w = wq;
+          o.dtype = CK_BF16;
+          o.scale = nullptr;
+          wq += (size_t)N * K * 2;
+        }
+      }
+  }
 
   const bool fused_head = use_fused_head(m);
   if (io.stage != kKvOnly) {
@@ -270,6 +338,16 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
     if (side != nullptr) {
       if (cudaEventRecord(side->join, ps) != cudaSuccess) return record_cuda_error();
       join_ev = side->join;
+    }
+    // the INT8 weights of the blocks, widened and scaled to bf16 as
+    // QuantizedLinear.forward does per call (cortex/quantization/calibrate.py:225-228);
+    // joined before the first block, after the cross attention
+    if (!deq.empty()) {
+      CK_TRY(dequant_int8(deq.data(), (int)deq.size(), ps));
+      if (side != nullptr) {
+        if (cudaEventRecord(side->deq, ps) != cudaSuccess) return record_cuda_error();
+        deq_ev = side->deq;
+      }
     }
   }
 
@@ -371,27 +449,33 @@ int forward_impl(const ck_model* m, const void* nid, const void* tb, const void*
       CK_TRY(lin(m, P(lay.att), BL, D, D, m->cross_out, D, CK_EPI_RESID, m->latents, D, L,
                  P(lay.lat), D, st));
     }
-    // 7. self-attention blocks
+    // 7. self-attention blocks (their dequantised weights join here)
+    if (deq_ev != nullptr && cudaStreamWaitEvent(st, deq_ev, 0) != cudaSuccess)
+      return record_cuda_error();
     for (int i = 0; i < m->num_layers; ++i) {
       const ck_block_weights& w = m->blocks[i];
+      const ck_linear_weight& w_qkv = bw[(size_t)i * 4];
+      const ck_linear_weight& w_out = bw[(size_t)i * 4 + 1];
+      const ck_linear_weight& w_mlp0 = bw[(size_t)i * 4 + 2];
+      const ck_linear_weight& w_mlp2 = bw[(size_t)i * 4 + 3];
       if (!x_ready)
         CK_TRY(row_norm(P(lay.lat), m->dtype, BL, (int32_t)D, D, w.norm_attn_w, w.norm_attn_b,
                         kLnEps, CK_NORM_LAYER, P(lay.x), D, st));
-      CK_TRY(lin(m, P(lay.x), BL, D, D, w.qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
+      CK_TRY(lin(m, P(lay.x), BL, D, D, w_qkv, 3 * D, CK_EPI_STORE, nullptr, 0, 0, P(lay.qkv),
                  3 * D, st));
       x_ready = false;
       CK_TRY(self_attention());
-      CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, w.out, D, P(lay.lat), D, 0, P(lay.lat),
+      CK_TRY(lin_resid_ln(m, P(lay.att), BL, D, w_out, D, P(lay.lat), D, 0, P(lay.lat),
                           w.norm_mlp_w, w.norm_mlp_b, P(lay.x), st));
-      CK_TRY(lin(m, P(lay.x), BL, D, D, w.mlp0, Hm, CK_EPI_GELU, nullptr, 0, 0, P(lay.hbuf), Hm,
+      CK_TRY(lin(m, P(lay.x), BL, D, D, w_mlp0, Hm, CK_EPI_GELU, nullptr, 0, 0, P(lay.hbuf), Hm,
                  st));
       if (i + 1 < m->num_layers) {
-        CK_TRY(lin_resid_ln(m, P(lay.hbuf), BL, Hm, w.mlp2, D, P(lay.lat), D, 0, P(lay.lat),
+        CK_TRY(lin_resid_ln(m, P(lay.hbuf), BL, Hm, w_mlp2, D, P(lay.lat), D, 0, P(lay.lat),
                             m->blocks[i + 1].norm_attn_w, m->blocks[i + 1].norm_attn_b, P(lay.x),
                             st));
         x_ready = true;
       } else {
-        CK_TRY(lin(m, P(lay.hbuf), BL, Hm, Hm, w.mlp2, D, CK_EPI_RESID, P(lay.lat), D, 0,
+        CK_TRY(lin(m, P(lay.hbuf), BL, Hm, Hm, w_mlp2, D, CK_EPI_RESID, P(lay.lat), D, 0,
                    P(lay.lat), D, st));
       }
     }

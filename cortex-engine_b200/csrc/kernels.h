@@ -130,6 +130,18 @@ int row_norm2(const void* x, int dtype, int64_t M, int32_t D, int64_t ldx, const
               const void* b1, const void* g2, const void* b2, float eps, void* y, int64_t ldy,
               cudaStream_t st);
 
+// INT8 weight dequantisation (dequant.cu): out[n, k] = bf16(float(w[n, k]) *
+// scale[n]) for a list of (N, K) matrices; K a multiple of 16, rows 16-byte
+// aligned.
+struct DequantSeg {
+  const int8_t* w;     // (N, K) int8, row stride ldw
+  const float* scale;  // (N,)
+  void* out;           // (N, K) bf16, row stride ldo
+  int64_t N, K, ldw, ldo;
+};
+bool dequant_seg_ok(const DequantSeg& g);
+int dequant_int8(const DequantSeg* segs, int n, cudaStream_t st);
+
 // packing and tokenizer (pack.cu, tokenizer.cu)
 size_t pack_workspace_bytes(int64_t E, int32_t B);
 // n_valid (device, may be NULL): events n_valid..E-1 are padding (pack.cu)

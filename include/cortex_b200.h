@@ -133,6 +133,15 @@ int ck_tokenize_packed(const void* n_emb, const void* t_emb, const void* v_emb, 
                        float eps, void* out, int64_t out_ld, int32_t* offsets, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* QuantizedLinear's weight (cortex/quantization/calibrate.py:225-228):
+ * out[n, k] = bf16(float(w_int8[n, k]) * scale[n]), the fp32 product rounded
+ * once, as (w.float() * s[:, None]).to(torch.bfloat16). w_int8 (N, K) with row
+ * stride ldw, out (N, K) bf16 with row stride ldo; K a multiple of 16, both
+ * 16-byte aligned (ldw a multiple of 16, ldo of 8). ck_forward applies it to
+ * the INT8 linears of the self-attention blocks once per call. */
+int ck_dequantize_int8(const void* w_int8, const float* scale, int64_t N, int64_t K, int64_t ldw,
+                       void* out, int64_t ldo, void* stream);
+
 /* ── 3. row norm ────────────────────────────────────────────────────────────
  * nn.LayerNorm (cortex/models/perceiver.py:51-52,97-98,143) or the RMSNorm of
  * rms_norm_linear_reference (cortex/kernels/fused_rmsnorm.py:86-108), fp32

@@ -219,6 +219,25 @@ def test_tokenize_packed_out_of_range_window_index():
     assert torch.equal(tok[:5], ref[[0, 1, 2, 4, 5]])
 
 
+@pytest.mark.parametrize("N,K", [(1536, 512), (512, 2048), (3, 16), (2304, 768)])
+def test_dequantize_int8_is_quantized_linears_weight(N, K):
+    """ck_dequantize_int8 against QuantizedLinear's expression
+    (w_int8.float() * scale[:, None]).to(bfloat16): bit-exact, every int8 value."""
+    from cortex import _lib as L
+
+    g = torch.Generator().manual_seed(N + K)
+    w = torch.randint(-128, 128, (N, K), dtype=torch.int8, generator=g)
+    w[0, : min(K, 256)] = torch.arange(-128, 128, dtype=torch.int16)[: min(K, 256)].to(torch.int8)
+    s = (torch.rand(N, generator=g) * 3e-2 + 1e-8).float()
+    ref = (w.float() * s[:, None]).to(torch.bfloat16)
+    wd, sd = w.to(DEV), s.to(DEV)
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=DEV)
+    rc = L.load().ck_dequantize_int8(wd.data_ptr(), sd.data_ptr(), N, K, K, out.data_ptr(), K,
+                                     L.stream_of(wd.device))
+    assert rc == 0, L.status_string(rc)
+    assert torch.equal(out.cpu(), ref)
+
+
 # ── row norm ─────────────────────────────────────────────────────────────────
 
 
