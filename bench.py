@@ -73,8 +73,6 @@ NCU_TRAFFIC = {
                             "(profiles/attn_ws_self_cfg1.md)"},
     ("cfg1", "tokenizer"): {"bytes": 1_310_000, "note": "the tokenizer launch: tables and "
                             "indices; the 16 MB of tokens stay in L2 (profiles/tokenize_cfg1.md)"},
-    ("cfg2", "gemm_store"): {"bytes": 9_230_000, "note": "layer 0's INT8 qkv_proj "
-                             "(profiles/gemm_tc_int8_qkv_cfg2.md)"},
 }
 
 

@@ -10,9 +10,9 @@
 // once per forward instead of once per 128-row tile of activations inside the
 // GEMM, and the GEMMs see the reference's own rounded weights.
 //
-// One launch covers up to kMaxSeg weight matrices (segments); a warp walks a
-// row at a time, 16 int8 values (one 16-byte load) per lane and step. The
-// work is HBM / L2 bound: K bytes read and 2K bytes written per row.
+// One launch covers up to kMaxSeg weight matrices (segments), walked as one
+// flat space of 16-value chunks (one 16-byte load each). The work is HBM / L2
+// bound: K bytes read and 2K bytes written per row.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -24,7 +24,7 @@ constexpr int kMaxSeg = 40;
 
 struct DeqLaunch {
   DequantSeg seg[kMaxSeg];
-  int64_t row_end[kMaxSeg];  // exclusive prefix of the segments' rows
+  int64_t chunk_end[kMaxSeg];  // inclusive prefix of the segments' 16-byte chunks
   int nseg;
 };
 
@@ -44,29 +44,48 @@ __device__ __forceinline__ void i8x16(const uint4 v, float* f) {
   }
 }
 
+// The segments' 16-value chunks as one flat index space, kUnroll chunks per
+// thread and step (independent loads in flight), consecutive threads on
+// consecutive chunks of a row.
+constexpr int kUnroll = 4;
+
 __global__ void __launch_bounds__(256) dequant_kernel(const __grid_constant__ DeqLaunch a) {
   grid_dep_wait();
   grid_dep_launch();
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t rows = a.row_end[a.nseg - 1];
-  int s = 0;
-  for (int64_t r = warp; r < rows; r += nwarps) {
-    while (r >= a.row_end[s]) ++s;  // rows only grow for a warp
-    const DequantSeg& g = a.seg[s];
-    const int64_t n = r - (s > 0 ? a.row_end[s - 1] : 0);
-    const float sc = g.scale[n];
-    const uint4* src = reinterpret_cast<const uint4*>(g.w + n * g.ldw);
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(g.out) + n * g.ldo);
-    for (int64_t c = lane; c < g.K / 16; c += 32) {
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  const int64_t total = a.chunk_end[a.nseg - 1];
+  int s = 0;  // a thread's chunks only grow
+  for (int64_t c0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c0 < total;
+       c0 += kUnroll * nthreads) {
+    uint4 v[kUnroll];
+    float sc[kUnroll];
+    __nv_bfloat16* dst[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t c = c0 + u * nthreads;
+      dst[u] = nullptr;
+      if (c < total) {
+        while (c >= a.chunk_end[s]) ++s;
+        const DequantSeg& g = a.seg[s];
+        const uint32_t q = (uint32_t)(c - (s > 0 ? a.chunk_end[s - 1] : 0));
+        const uint32_t kc = (uint32_t)(g.K / 16);
+        const uint32_t row = q / kc, col = q - row * kc;
+        v[u] = __ldg(reinterpret_cast<const uint4*>(g.w + (int64_t)row * g.ldw) + col);
+        sc[u] = __ldg(g.scale + row);
+        dst[u] = reinterpret_cast<__nv_bfloat16*>(g.out) + (int64_t)row * g.ldo + 16 * col;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (dst[u] == nullptr) continue;
       float f[16];
-      i8x16(__ldg(src + c), f);
-      dst[2 * c] = make_uint4(cvt_bf16x2(f[0] * sc, f[1] * sc), cvt_bf16x2(f[2] * sc, f[3] * sc),
-                              cvt_bf16x2(f[4] * sc, f[5] * sc), cvt_bf16x2(f[6] * sc, f[7] * sc));
-      dst[2 * c + 1] =
-          make_uint4(cvt_bf16x2(f[8] * sc, f[9] * sc), cvt_bf16x2(f[10] * sc, f[11] * sc),
-                     cvt_bf16x2(f[12] * sc, f[13] * sc), cvt_bf16x2(f[14] * sc, f[15] * sc));
+      i8x16(v[u], f);
+      const float k = sc[u];
+      uint4* o = reinterpret_cast<uint4*>(dst[u]);
+      o[0] = make_uint4(cvt_bf16x2(f[0] * k, f[1] * k), cvt_bf16x2(f[2] * k, f[3] * k),
+                        cvt_bf16x2(f[4] * k, f[5] * k), cvt_bf16x2(f[6] * k, f[7] * k));
+      o[1] = make_uint4(cvt_bf16x2(f[8] * k, f[9] * k), cvt_bf16x2(f[10] * k, f[11] * k),
+                        cvt_bf16x2(f[12] * k, f[13] * k), cvt_bf16x2(f[14] * k, f[15] * k));
     }
   }
 }
@@ -77,23 +96,23 @@ bool dequant_seg_ok(const DequantSeg& g) {
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   return g.w != nullptr && g.scale != nullptr && g.out != nullptr && g.N > 0 && g.K > 0 &&
          g.K % 16 == 0 && g.ldw >= g.K && g.ldo >= g.K && g.ldw % 16 == 0 && g.ldo % 8 == 0 &&
-         al16(g.w) && al16(g.out);
+         al16(g.w) && al16(g.out) && g.N * (g.K / 16) < (int64_t(1) << 32);
 }
 
 int dequant_int8(const DequantSeg* segs, int n, cudaStream_t st) {
   for (int i0 = 0; i0 < n; i0 += kMaxSeg) {
     DeqLaunch a;
     a.nseg = n - i0 < kMaxSeg ? n - i0 : kMaxSeg;
-    int64_t rows = 0;
+    int64_t chunks = 0;
     for (int i = 0; i < a.nseg; ++i) {
       const DequantSeg& g = segs[i0 + i];
       if (!dequant_seg_ok(g)) return CK_ERR_INVALID_ARG;
       a.seg[i] = g;
-      rows += g.N;
-      a.row_end[i] = rows;
+      chunks += g.N * (g.K / 16);
+      a.chunk_end[i] = chunks;
     }
-    // a resident grid (8 CTAs of 8 warps per SM), fewer for small jobs
-    int64_t blocks = (rows + 7) / 8;
+    // a resident grid (8 CTAs of 256 threads per SM), fewer for small jobs
+    int64_t blocks = (chunks + 256 * kUnroll - 1) / (256 * kUnroll);
     const int64_t cap = 8 * (int64_t)num_sms();
     if (blocks > cap) blocks = cap;
     const int rc = launch_pdl(dequant_kernel, dim3((unsigned)blocks), dim3(256), 0, st, a);
