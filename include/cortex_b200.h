@@ -272,6 +272,10 @@ typedef struct ck_model {
   ck_linear_weight head_q, head_kv, head_out;
 } ck_model;
 
+/* The workspace holds the forward's intermediates and, for bf16 models whose
+ * self-attention blocks carry INT8 linears, their weights dequantised to bf16
+ * (bf16(float(w_int8) * scale), QuantizedLinear's rounding) once per call, on
+ * which the blocks' GEMMs run. Contents arbitrary on entry. */
 size_t ck_forward_workspace_bytes(const ck_model* m, int64_t E, int32_t B);
 int ck_forward(const ck_model* m, const void* neuron_ids, const void* time_bins,
                const void* values, const void* batch_indices, int idx_dtype, int64_t E,
