@@ -13,6 +13,15 @@
 // (device count, padded batches) events n_valid..E-1 are padding: their ids
 // are not read and their rows are written as zeros, which keeps every row a
 // later kernel may touch finite.
+//
+// tokenize_packed also does _pack_events' index work (cortex/models/cortex.py:
+// 125-165) for the forward: with the batch indices sorted, the packed row of
+// event e is e and window b starts at its first event, so each event's group
+// writes the offsets of the windows that begin at it and its token to row e,
+// and each block records whether it saw an index out of order or out of
+// [0, B). tok_fixup_kernel, launched after it, reads those flags and, only
+// when one is set, redoes the packing as a stable counting sort and tokenizes
+// every event again into its packed row.
 #include <type_traits>
 
 #include "common.cuh"
