@@ -238,6 +238,29 @@ def test_dequantize_int8_is_quantized_linears_weight(N, K):
     assert torch.equal(out.cpu(), ref)
 
 
+def test_dequantize_int8_strided_rows_and_rejections():
+    """Row strides wider than K on both sides (a weight slice, an output slice)
+    leave the padding untouched; K not a multiple of 16 is rejected."""
+    from cortex import _lib as L
+
+    N, K = 300, 512
+    g = torch.Generator().manual_seed(7)
+    wide = torch.randint(-128, 128, (N, K + 32), dtype=torch.int8, generator=g)
+    s = torch.rand(N, generator=g) * 1e-2
+    ref = (wide[:, :K].float() * s[:, None]).to(torch.bfloat16)
+    wd, sd = wide.to(DEV), s.to(DEV)
+    out = torch.full((N, K + 8), 7.0, dtype=torch.bfloat16, device=DEV)
+    lib = L.load()
+    rc = lib.ck_dequantize_int8(wd.data_ptr(), sd.data_ptr(), N, K, K + 32, out.data_ptr(), K + 8,
+                                L.stream_of(wd.device))
+    assert rc == 0, L.status_string(rc)
+    assert torch.equal(out[:, :K].cpu(), ref)
+    assert bool((out[:, K:] == 7.0).all())
+    rc = lib.ck_dequantize_int8(wd.data_ptr(), sd.data_ptr(), N, 40, K + 32, out.data_ptr(), K + 8,
+                                L.stream_of(wd.device))
+    assert rc == L.CK_ERR_INVALID_ARG
+
+
 # ── row norm ─────────────────────────────────────────────────────────────────
 
 
