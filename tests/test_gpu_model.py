@@ -186,6 +186,37 @@ def test_sharded_decode_is_the_full_batch_decode(name, batch):
             assert torch.equal(torch.cat(parts), full), world
 
 
+@pytest.mark.parametrize("name", ["cfg2", "cfg4"])
+def test_int8_forward_is_the_bf16_forward_on_dequantised_weights(name):
+    """QuantizedLinear.forward dequantises per call: (w_int8.float() * s).to(bf16)
+    then a bf16 linear. The INT8 model's forward must equal, bit for bit, the
+    forward of a bf16 model whose block linears hold exactly those weights
+    (dequantised here by torch)."""
+    from cortex.quantization.calibrate import QuantizedLinear
+    from cortex.workloads import make_inputs
+
+    wl, model = _model(name)
+    _, ref_model = _model(name)  # the same seeded weights and INT8 conversion
+    n = 0
+    for mod_name, mod in list(ref_model.named_modules()):
+        for child_name, child in list(mod.named_children()):
+            if isinstance(child, QuantizedLinear):
+                lin = torch.nn.Linear(child.in_features, child.out_features, bias=False,
+                                      device=DEV, dtype=torch.bfloat16)
+                with torch.no_grad():
+                    lin.weight.copy_((child.weight_int8.float()
+                                      * child.weight_scale.float()[:, None]).to(torch.bfloat16))
+                setattr(mod, child_name, lin)
+                n += 1
+    assert n == 4 * wl.config.num_layers
+    inp, _ = make_inputs(wl, seed=21, batch=8)
+    cols = ("neuron_ids", "time_bins", "values", "batch_indices")
+    with torch.no_grad():
+        y8 = model(*(inp[k].to(DEV) for k in cols))["behavior"]
+        y16 = ref_model(*(inp[k].to(DEV) for k in cols))["behavior"]
+    assert torch.equal(y8, y16)
+
+
 def test_interleaved_events_and_int32_indices():
     from cortex.workloads import make_inputs
 
