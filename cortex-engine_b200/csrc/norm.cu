@@ -157,7 +157,7 @@ __global__ void row_norm_kernel(const T* x, int64_t M, int D, int64_t ldx, const
 // 16-byte vectors per lane, gamma / beta as 16-byte vectors. Same two-pass
 // statistics as row_norm_kernel; TWO applies a second LayerNorm after rounding.
 template <int MAXV, int G, bool TWO>
-__global__ void __launch_bounds__(256, 2) layer_norm_bf16_kernel(
+__global__ void __launch_bounds__(256, MAXV <= 6 ? 3 : 2) layer_norm_bf16_kernel(
     const __nv_bfloat16* x, int64_t M, int D, int64_t ldx, const __nv_bfloat16* g1,
     const __nv_bfloat16* b1, const __nv_bfloat16* g2, const __nv_bfloat16* b2, float eps,
     __nv_bfloat16* y, int64_t ldy) {
@@ -289,6 +289,9 @@ int dispatch_norm(const void* x, int64_t M, int D, int64_t ldx, const void* g1, 
       // 8 lanes per row (4 rows per warp) and up to 8 vectors per lane: all rows
       // of a Cortex-S latent batch are loaded in a single wave of the grid
       if (nvec <= 64) return launch_ln_fast<8, 8>(x, M, D, ldx, g1, b1, g2, b2, eps, two, y, ldy, st);
+      // D = 768 (Cortex-M): 16 lanes x 6 vectors, two rows per warp, three CTAs
+      // per SM, so that more rows are in flight than with a warp per row
+      if (nvec <= 96) return launch_ln_fast<6, 16>(x, M, D, ldx, g1, b1, g2, b2, eps, two, y, ldy, st);
       if (nvec <= 128) return launch_ln_fast<4, 32>(x, M, D, ldx, g1, b1, g2, b2, eps, two, y, ldy, st);
     }
   }
