@@ -209,6 +209,7 @@ __device__ __forceinline__ float rcp_approx(float x) {
 // x / 2 + |x| (1/2 - t) for either sign of x, with no select. The 16 value
 // pairs go through each step together (paired fp32 instructions), so every
 // step has 16 independent operations to hide the latency of the previous one.
+template <bool KEEP_TAIL = false>
 __device__ __forceinline__ void gelu32_pairs(float* v) {
   unsigned long long y[16], q[16];
 #pragma unroll
@@ -244,7 +245,11 @@ __device__ __forceinline__ void gelu32_pairs(float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const unsigned long long h = ffma2(q[i], f2pk(-1.f, -1.f), half);  // erf(|x|/sqrt 2) / 2
-    f2up(ffma2(y[i], h, fmul2(f2pk(v[2 * i], v[2 * i + 1]), half)), v[2 * i], v[2 * i + 1]);
+    float r0, r1;
+    f2up(ffma2(y[i], h, fmul2(f2pk(v[2 * i], v[2 * i + 1]), half)), r0, r1);
+    // KEEP_TAIL: values below kGeluTail stay as they are, for gelu_tail
+    v[2 * i] = (KEEP_TAIL && v[2 * i] < kGeluTail) ? v[2 * i] : r0;
+    v[2 * i + 1] = (KEEP_TAIL && v[2 * i + 1] < kGeluTail) ? v[2 * i + 1] : r1;
   }
 }
 
@@ -260,13 +265,13 @@ __device__ __forceinline__ void gelu32(float* v) {
 #pragma unroll
   for (int i = 1; i < 32; ++i) lo = fminf(lo, v[i]);
   if (__any_sync(0xffffffffu, lo < kGeluTail)) {
+    // the polynomial form on the paired pipe for every value but the tail
+    // ones, which keep x (GELU itself is never below -0.2) and then take the
+    // library-erf form
+    gelu32_pairs<true>(v);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      if (v[i] < kGeluTail)
-        v[i] = gelu_tail(v[i]);
-      else
-        v[i] = gelu_as(v[i]);
-    }
+    for (int i = 0; i < 32; ++i)
+      if (v[i] < kGeluTail) v[i] = gelu_tail(v[i]);
   } else {
     gelu32_pairs(v);
   }
