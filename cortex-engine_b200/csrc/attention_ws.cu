@@ -371,6 +371,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
           tmem_ld32(tmem_oh + q * 32, o0);
           tmem_ld32(tmem_oh + 64 + q * 32, o1);
           tc_wait_ld();
+          if (q + 1 == DH / 32) {  // all of O read: the next item's products may start
+            tc_fence_before();
+            mbar_arrive(o_free);
+          }
           if (pend_dst != nullptr) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) o0[i] = fmaf(o0[i], f0, o1[i] * f1);
@@ -379,9 +383,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
               reinterpret_cast<uint4*>(pend_dst)[4 * q + c] = pack8(o0 + 8 * c);
           }
         }
-        tc_fence_before();
       }
-      mbar_arrive(o_free);  // O_0, O_1 may be overwritten by the next item
+      if (kh == 1) mbar_arrive(o_free);  // O_0, O_1 may be overwritten by the next item
       ++nout;
       pend = false;
       return true;
