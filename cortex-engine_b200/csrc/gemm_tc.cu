@@ -887,6 +887,7 @@ int dispatch_epi(int epi, int fuse, const CUtensorMap& ta, const CUtensorMap& tb
     if constexpr (BN == 256 && WMODE == W_BF16_NK) {
       if (epi == CK_EPI_STORE) return launch_gemm<BN, WMODE, CK_EPI_STORE, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
       if (epi == CK_EPI_GELU) return launch_gemm<BN, WMODE, CK_EPI_GELU, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
+      if (epi == CK_EPI_RESID) return launch_gemm<BN, WMODE, CK_EPI_RESID, FUSE_NONE, true>(ta, tb, ty0, ty2, tr, a, st);
     }
     return CK_ERR_UNSUPPORTED;
   }
@@ -934,14 +935,17 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t lda, int w_dtype, int w_lay
   return true;
 }
 
-// 2-SM pairs by default only for long K: measured on B200 (bf16, 256-wide N
-// tiles) they take 8 % off 16384 x 2048 x 2048 and 2 % off 8192 x 2048 x 1024,
-// but nothing off K = 512 shapes, where the split last round is the better
-// tool. CK_GEMM_PAIR=1 / 0 forces them on / off.
-bool gemm_pair_enabled(int64_t K) {
+// 2-SM pairs by default for long K, and for K >= 768 on tall A: measured on
+// B200 (bf16, 256-wide N tiles) they take 8 % off 16384 x 2048 x 2048, 2 % off
+// 8192 x 2048 x 1024, and 4-7 % off the Cortex-M forward from 16384 rows up
+// (K = 768 and 3072; at 8192 rows they cost 0.6 %), but nothing off K = 512
+// shapes (the Cortex-S forwards at 8192 and 65536 rows), where the weight
+// prefetch and the split last round are the better tools. CK_GEMM_PAIR=1 / 0
+// forces them on / off.
+bool gemm_pair_enabled(int64_t M, int64_t K) {
   const char* v = std::getenv("CK_GEMM_PAIR");
   if (v != nullptr) return std::strcmp(v, "0") != 0;
-  return K >= 2048;
+  return K >= 2048 || (K >= 768 && M >= 16384);
 }
 
 bool gemm_split_enabled() {
@@ -1003,11 +1007,12 @@ int gemm_tc(const void* A, int64_t M, int64_t K, int64_t lda, const void* W, int
   }
 
   // 2-SM pairs (256-row tiles, B split over the pair): bf16 (N, K) weights, a
-  // store or GELU epilogue, no fusion, 256-wide N tiles, long K (see
-  // gemm_pair_enabled). The schedule then walks 256-row tiles.
+  // store, GELU or residual epilogue, no fusion, 256-wide N tiles (see
+  // gemm_pair_enabled for the shapes). The schedule then walks 256-row tiles.
   bool pair = false;
   if (fuse == gemm::FUSE_NONE && w_dtype == CK_BF16 && w_layout == CK_W_NK && BN == 256 &&
-      (epi == CK_EPI_STORE || epi == CK_EPI_GELU) && a.num_m_tiles >= 2 && gemm_pair_enabled(K)) {
+      (epi == CK_EPI_STORE || epi == CK_EPI_GELU || epi == CK_EPI_RESID) && a.num_m_tiles >= 2 &&
+      gemm_pair_enabled(M, K)) {
     pair = true;
     a.num_m_tiles = (a.num_m_tiles + 1) / 2;
     a.num_tiles = a.num_m_tiles * a.num_n_tiles;

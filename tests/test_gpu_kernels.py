@@ -385,25 +385,36 @@ def test_split_last_round_is_bit_identical(monkeypatch, M, N, epi):
 
 @pytest.mark.parametrize("M,K,N,epi", [(8192, 512, 1536, "store"), (8192, 512, 2048, "gelu"),
                                        (16384, 512, 1024, "store"), (300, 768, 2304, "store"),
-                                       (256, 512, 512, "gelu"), (1000, 2048, 512, "store")])
+                                       (256, 512, 512, "gelu"), (1000, 2048, 512, "store"),
+                                       (8192, 3072, 768, "resid"), (1000, 768, 768, "resid"),
+                                       (4096, 2048, 768, "resid_mod")])
 def test_pair_mma_matches_single_cta(monkeypatch, M, K, N, epi):
     """2-SM tiles (a CTA pair, 256 rows, B split over the pair, cta_group::2
-    MMAs issued by the even CTA) against one-CTA tiles and the fp32 product."""
+    MMAs issued by the even CTA) against one-CTA tiles and the fp32 product;
+    the residual epilogue also with a broadcast (row-periodic) residual."""
     from cortex import _lib as L
     from cortex.kernels import _ops
 
     torch.manual_seed(M + K + N)
     x = torch.randn(M, K, dtype=torch.bfloat16)
     w = (torch.randn(N, K) / math.sqrt(K)).to(torch.bfloat16)
-    e = L.CK_EPI_GELU if epi == "gelu" else L.CK_EPI_STORE
+    e = {"gelu": L.CK_EPI_GELU, "store": L.CK_EPI_STORE}.get(epi, L.CK_EPI_RESID)
+    mod = 512 if epi == "resid_mod" else 0
+    res = torch.randn(mod or M, N).to(torch.bfloat16) if e == L.CK_EPI_RESID else None
+    kw = dict(epi=e)
+    if res is not None:
+        kw.update(aux=res.to(DEV), aux_row_mod=mod)
     monkeypatch.setenv("CK_GEMM_PAIR", "1")
-    pair = _ops.linear(x.to(DEV), w.to(DEV), epi=e)
+    pair = _ops.linear(x.to(DEV), w.to(DEV), **kw)
     _status_ok()
     monkeypatch.setenv("CK_GEMM_PAIR", "0")
-    single = _ops.linear(x.to(DEV), w.to(DEV), epi=e)
+    single = _ops.linear(x.to(DEV), w.to(DEV), **kw)
     ref = _gemm_ref(x, w)
     if epi == "gelu":
         ref = torch.nn.functional.gelu(ref.to(torch.bfloat16).float())
+    if res is not None:
+        rows = torch.arange(M) % mod if mod else torch.arange(M)
+        ref = ref.to(torch.bfloat16).float() + res.float()[rows]
     rel = ((pair.float().cpu() - ref).norm() / ref.norm()).item()
     assert rel < 5e-3, rel
     assert torch.equal(pair, single)
