@@ -15,9 +15,9 @@ One runner serves one (device, stream). Its graphs bake in the weight pointers
 of the model description they were captured with: when the description
 changes (weights moved, recast or replaced, modules swapped) the runner drops
 its graphs. They also bake in the kernel selection of their capture: the
-library's environment switches (CK_PDL, CK_HEAD_FUSED, CK_NORM_FOLD,
-CK_LN_FUSE, CK_CHAIN) are read then, and ``BatchRunner.invalidate()`` makes later
-batches capture afresh.
+library's environment switches (CK_PDL, CK_HEAD_FUSED, CK_LN_FUSE, CK_SIDE,
+CK_GEMM_PAIR, CK_GEMM_SPLIT) are read then, and ``BatchRunner.invalidate()``
+makes later batches capture afresh.
 """
 
 from __future__ import annotations

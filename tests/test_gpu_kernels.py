@@ -537,6 +537,32 @@ def test_norm_linear_fused_single_launch(M, K, N, wkind, with_bias):
     torch.testing.assert_close(out, ref, rtol=2e-2, atol=5e-2 * ref.abs().max().item() / 8)
 
 
+def test_norm_linear_fused_strided_rows():
+    """The one-launch kernel takes A's rows at the caller's row stride (a
+    column slice of a wider tensor), with a ragged last row block."""
+    torch.manual_seed(5)
+    M, K, N, ld = 300, 512, 512, 768
+    xw = torch.randn(M, ld, dtype=torch.bfloat16)
+    x = xw[:, 64:64 + K]
+    g = (torch.rand(K) + 0.5).to(torch.bfloat16)
+    w = torch.randn(K, N, dtype=torch.bfloat16) / math.sqrt(K)
+    xd, gd, wd = xw.to(DEV), g.to(DEV), w.to(DEV)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    n0 = L.load().ck_launch_count()
+    rc = L.load().ck_norm_linear(xd.data_ptr() + 64 * 2, L.CK_BF16, M, K, ld, gd.data_ptr(), None,
+                                 1e-6, L.CK_NORM_RMS, wd.data_ptr(), L.CK_BF16, L.CK_W_KN, N, N,
+                                 None, L.CK_EPI_STORE, None, 0, 0, y.data_ptr(), N, None, 0,
+                                 L.stream_of(xd.device))
+    assert rc == L.CK_OK, L.status_string(rc)
+    assert L.load().ck_launch_count() - n0 == 1
+    _status_ok()
+    contiguous = _norm_linear_call(x.contiguous().to(DEV), gd, wd, None, None)[1]
+    assert torch.equal(y, contiguous)
+    ref = O.rms_norm_linear(x, g, w, None).float()
+    rel = ((y.float().cpu() - ref).norm() / ref.norm()).item()
+    assert rel <= 1e-2, rel
+
+
 def test_norm_linear_fallback_asks_for_workspace():
     """Calls the one-launch path does not take (K not 16-byte aligned here)
     return CK_ERR_WORKSPACE without launching when no workspace is given."""
