@@ -151,6 +151,15 @@ __device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsign
   return d;
 }
 
+// bf16x2 add, round to nearest even. For bf16 a and b this equals the fp32 sum
+// rounded to bf16 (torch's bf16 add): fp32 holds 24 >= 2 * 8 + 2 significand
+// bits, so rounding first to fp32 and then to bf16 gives the single rounding.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // bf16 pair conversions: one cvt for two values (round to nearest even).
 __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
   uint32_t r;

@@ -67,6 +67,20 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& p, int m, int n0, 
       for (int i = 0; i < 32; ++i) v[i] *= (n0 + i < p.N) ? __ldg(p.w_scale + n0 + i) : 0.f;
     }
   }
+  if ((EPI == CK_EPI_RESID || EPI == CK_EPI_BIAS) && full && m < p.M) {
+    // bf16(bf16(acc) + r) as torch's bf16 add computes it, one bf16x2 add per pair
+    const __nv_bfloat16* src =
+        EPI == CK_EPI_RESID ? p.aux + residual_row(p, m) * p.ld_aux + n0 : p.aux + n0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 u = res != nullptr ? res[c] : __ldg(reinterpret_cast<const uint4*>(src) + c);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        out[4 * c + j] = add_bf16x2(cvt_bf16x2(v[8 * c + 2 * j], v[8 * c + 2 * j + 1]), w[j]);
+    }
+    return;
+  }
   if (EPI != CK_EPI_STORE) {
 #pragma unroll
     for (int i = 0; i < 32; i += 2) rbf2(v[i], v[i + 1]);

@@ -541,23 +541,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, WMODE, FUSE, EPI, PAIR>::NUM_THREA
           if (C::LN) {
             // statistics of the values as stored (bf16), shifted by the
             // segment's first value so the sum of squares does not cancel
+            if (c == 0) st_shift = bf16_lo(packed[0]);
+            // (even, odd) columns in the two lanes of paired fp32 sums
+            const unsigned long long nshift = f2pk(-st_shift, -st_shift);
+            unsigned long long s1 = f2pk(0.f, 0.f), s2 = f2pk(0.f, 0.f);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              cur[2 * i] = bf16_lo(packed[i]);
-              cur[2 * i + 1] = bf16_hi(packed[i]);
+              const bool ok0 = n0 + 2 * i < p.N, ok1 = n0 + 2 * i + 1 < p.N;
+              const unsigned long long d =
+                  fadd2(f2pk(ok0 ? bf16_lo(packed[i]) : st_shift, ok1 ? bf16_hi(packed[i]) : st_shift),
+                        nshift);
+              s1 = fadd2(s1, d);
+              s2 = ffma2(d, d, s2);
             }
-            if (c == 0) st_shift = cur[0];
-            float s1a = 0.f, s1b = 0.f, s2a = 0.f, s2b = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const bool ok0 = n0 + i < p.N, ok1 = n0 + i + 1 < p.N;
-              const float d0 = ok0 ? cur[i] - st_shift : 0.f;
-              const float d1 = ok1 ? cur[i + 1] - st_shift : 0.f;
-              s1a += d0;
-              s1b += d1;
-              s2a = fmaf(d0, d0, s2a);
-              s2b = fmaf(d1, d1, s2b);
-            }
+            float s1a, s1b, s2a, s2b;
+            f2up(s1, s1a, s1b);
+            f2up(s2, s2a, s2b);
             st_s1 += s1a + s1b;
             st_s2 += s2a + s2b;
           }
