@@ -213,3 +213,29 @@ def test_int8_to_bf16_bit_trick_is_exact_for_every_byte():
     r = b[0] | (b[2] << 8) | (b[1] << 16) | (b[3] << 24)
     assert (r & 0xFF, (r >> 16) & 0xFF) == (b[0], b[1])
     assert ((r >> 8) & 0xFF, (r >> 24) & 0xFF) == (b[2], b[3])
+
+
+def _rn_bf16(x: np.ndarray) -> np.ndarray:
+    """Round float64 values (normal range) to the nearest bf16, ties to even:
+    8 significant bits, the rounding done once on the exact value."""
+    m, e = np.frexp(x)  # x = m * 2**e, 0.5 <= |m| < 1
+    return np.ldexp(np.round(m * 256.0) / 256.0, e)  # np.round: half to even
+
+
+def test_bf16x2_add_equals_fp32_add_then_round():
+    """The GEMM's residual and bias epilogues add bf16 pairs with one
+    add.rn.bf16x2 (gemm_common.cuh): the exact sum of two bf16 values rounded
+    once to bf16. torch's bf16 add rounds the fp32 sum to bf16 instead. The two
+    agree because fp32 keeps 24 >= 2 * 8 + 2 significand bits. Checked on
+    random bf16 pairs whose exponents differ by up to 40 (their float64 sum is
+    then exact), with cancellations and ties to even among them."""
+    rng = np.random.default_rng(11)
+    n = 1 << 20
+    a = torch.from_numpy(rng.standard_normal(n) * np.exp2(rng.integers(-20, 21, n))).to(torch.bfloat16)
+    b = torch.from_numpy(rng.standard_normal(n) * np.exp2(rng.integers(-20, 21, n))).to(torch.bfloat16)
+    b[: n // 8] = -a[: n // 8] * (1 + torch.from_numpy(rng.integers(-3, 4, n // 8) / 256.0)).to(torch.bfloat16)
+    torch_sum = (a.float() + b.float()).to(torch.bfloat16).double().numpy()
+    exact = a.double().numpy() + b.double().numpy()
+    nz = exact != 0
+    ref = np.where(nz, _rn_bf16(np.where(nz, exact, 1.0)), 0.0)
+    assert np.array_equal(torch_sum, ref)
