@@ -239,3 +239,37 @@ def test_bf16x2_add_equals_fp32_add_then_round():
     nz = exact != 0
     ref = np.where(nz, _rn_bf16(np.where(nz, exact, 1.0)), 0.0)
     assert np.array_equal(torch_sum, ref)
+
+
+def test_bench_flop_accounting_matches_the_per_window_figures():
+    """bench.py's algorithmic FLOPs per kernel class (the roofline numerators)
+    for cfg1: per window kv_proj 0.537 G, cross-attention QK^T + PV 0.268 G,
+    cross out_proj 0.134 G and 7 self-attention blocks of 1.745 G (qkv 0.403,
+    attention 0.134, out_proj 0.134, MLP 1.074), plus q_proj 0.134 G once per
+    batch (it acts on the batch-invariant latent parameter). The behaviour
+    head's kv_proj is not counted: the fused head never computes it."""
+    import importlib.util
+
+    from cortex.workloads import WORKLOADS
+
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    wl = WORKLOADS["cfg1"]
+    B, E = 32, 32 * 512
+    w = bench.forward_work(wl, B, E, 8, {})
+    D, L, Hm, layers = 512, 256, 2048, 7
+    per_window = (2 * 512 * D * 2 * D + 4 * L * 512 * D + 2 * L * D * D
+                  + layers * (2 * L * D * 3 * D + 4 * L * L * D + 2 * L * D * D + 4 * L * D * Hm))
+    q_proj = 2 * L * D * D
+    assert abs(per_window / 1e9 - (0.537 + 0.268 + 0.134 + 7 * 1.745)) < 0.01
+    tensor = sum(v[1] for k, v in w.items() if not k.startswith("_") and v[0] == "tensor")
+    assert tensor == B * per_window + q_proj
+    assert w["gemm_resid"][1] == B * (2 * L * D * D + layers * (2 * L * D * D + 2 * L * Hm * D))
+    assert w["attention"][1] == B * (4 * L * 512 * D + layers * 4 * L * L * D)
+    # bench.py's class names for the forward's kernels
+    assert bench.kernel_class("gemm_tc_kernel<256, 0, 2, 3, 0>") == "gemm_resid"
+    assert bench.kernel_class("gemm_tc_kernel<256, 0, 1, 0, 0>") == "gemm_gelu"
+    assert bench.kernel_class("gemm_tc_kernel<256, 0, 0, 0, 1>") == "gemm_store"
+    assert bench.kernel_class("attn_ws_kernel") == "attention"
+    assert bench.kernel_class("tokenize_kernel<__nv_bfloat16, 8, 4, 1, 16>") == "tokenizer"
